@@ -1,0 +1,144 @@
+/*
+ * rt_attention.h -- C ABI of the B200 (sm_100a) Relational-Transformer masked
+ * attention library (libtributary_b200.so).
+ *
+ * The reference computes this path in JAX:
+ *   - the masks:    build_attention_masks          confluence/confluence/model.py:201-264
+ *   - permutation:  GatedAttentionSublayer          confluence/confluence/layers.py:139-152
+ *   - the core:     QKNormedMultiHeadAttention      confluence/confluence/layers.py:82-97
+ *                   (logits, -1e9 fill, softmax, PV) and its jax autodiff backward
+ *                   (jax.value_and_grad, confluence/confluence/train.py:209).
+ * The reference has no native operator for it; these entry points are what an
+ * XLA FFI custom call (or ctypes, cgo, ...) binds in place of those lines.
+ *
+ * Conventions
+ *   - Every call is stream-ordered on `stream` (a cudaStream_t passed as
+ *     void*, NULL = legacy default stream) and returns an rt_status.
+ *   - The caller owns every buffer; all pointers are device pointers unless
+ *     stated otherwise. Nothing here allocates device memory.
+ *   - Attention tensors are bf16 (passed as uint16_t bit patterns), laid out
+ *     [batch][heads][seq_len][head_dim] contiguous, 16-byte aligned.
+ *   - Token order is the *permuted* order of the reference (x_perm = x[perm]):
+ *     q/k/v row i belongs to original cell perm[b][i].
+ *   - Tiles are 128 x 128 in that permuted order.
+ *   - Device-side bounded waits never hang: a wait that runs out sets a
+ *     sticky device status, read with rt_device_status().
+ */
+#ifndef RT_ATTENTION_H
+#define RT_ATTENTION_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum rt_status {
+  RT_OK = 0,
+  RT_ERR_INVALID_ARGUMENT = 1, /* bad shape, null or misaligned pointer, bad kind */
+  RT_ERR_UNSUPPORTED = 2,      /* valid but not implemented (e.g. head_dim) */
+  RT_ERR_CUDA = 3,             /* a CUDA runtime / driver call or launch failed */
+  RT_ERR_TIMEOUT = 4,          /* a device-side bounded wait ran out */
+  RT_ERR_WORKSPACE = 5,        /* caller-provided buffer too small */
+  RT_ERR_DEVICE = 6            /* no usable sm_100 device */
+} rt_status;
+
+/* Mask kinds. Reference names (model.py:233-245): outbound == feature,
+ * inbound == neighbor. FULL (every non-padding pair, plus the diagonal) is
+ * not in the reference; it is the fourth benchmark kind. */
+typedef enum rt_mask_kind {
+  RT_MASK_COLUMN = 0,   /* col_i == col_j                       */
+  RT_MASK_FEATURE = 1,  /* row_i == row_j || fk_adj[row_i][row_j] */
+  RT_MASK_NEIGHBOR = 2, /* fk_adj[row_j][row_i]                  */
+  RT_MASK_FULL = 3      /* valid                                 */
+} rt_mask_kind;
+/* every kind is then ANDed with (!pad_i && !pad_j) and ORed with the
+ * diagonal i == j, exactly as model.py:248-262 */
+
+#define RT_TILE 128
+
+/* Tile plan: the prepass output for one (batch, mask kind, permutation).
+ * All arrays are device memory carved from one caller buffer by
+ * rt_tile_plan_bind(). T = ceil(seq_len / 128), W = ceil(T / 32). */
+typedef struct rt_tile_plan {
+  int32_t batch;
+  int32_t seq_len;
+  int32_t max_rows;
+  int32_t tiles;           /* T */
+  int32_t words;           /* W */
+  uint32_t* live_bits;     /* [batch][T][W]   bit kt of row (b,qt): tile has a true element */
+  uint32_t* full_bits;     /* [batch][T][W]   tile is entirely in range and entirely true  */
+  int32_t* q2k_ptr;        /* [batch*T + 1]   CSR row pointers over (b, qt)                */
+  int32_t* q2k_idx;        /* [batch*T*T]     live kt ascending; bit 31 = fully live       */
+  int32_t* k2q_ptr;        /* [batch*T + 1]   CSR row pointers over (b, kt)                */
+  int32_t* k2q_idx;        /* [batch*T*T]     live qt ascending; bit 31 = fully live       */
+  uint32_t* tile_masks;    /* [batch][T][T][128][4]  element bits, query-major (partial tiles) */
+  uint32_t* tile_masks_t;  /* [batch][T][T][128][4]  element bits, key-major   (partial tiles) */
+  uint32_t* fk_bits;       /* [batch][max_rows][ceil(max_rows/32)]  packed adjacency (scratch) */
+  int32_t* nnz;            /* [1] number of live tiles over the batch                         */
+} rt_tile_plan;
+
+/* Bytes of device memory a tile plan needs. */
+size_t rt_tile_plan_bytes(int32_t batch, int32_t seq_len, int32_t max_rows);
+
+/* Host-only: carve `buffer` (device memory, 256-byte aligned, `bytes` long)
+ * into a plan. No device work. */
+int rt_tile_plan_bind(void* buffer, size_t bytes, int32_t batch, int32_t seq_len,
+                      int32_t max_rows, rt_tile_plan* plan);
+
+/* Prepass: replaces build_attention_masks (model.py:201-264) plus the mask
+ * permutation of layers.py:144-152 for one kind. Inputs are the headwater
+ * batch tensors (headwater/src/python.rs:17-91):
+ *   perm        [batch][seq_len] uint16  (col_perm / out_perm / in_perm)
+ *   seq_row_ids [batch][seq_len] uint16
+ *   column_ids  [batch][seq_len] int32
+ *   is_padding  [batch][seq_len] uint8
+ *   fk_adj      [batch][max_rows][max_rows] uint8, fk_adj[child][parent]
+ * Row ids >= max_rows are clamped to max_rows-1 (jax's gather semantics).
+ * Fills every array of `plan`. */
+int rt_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids,
+                       const int32_t* column_ids, const uint8_t* is_padding,
+                       const uint8_t* fk_adj, int32_t batch, int32_t seq_len,
+                       int32_t max_rows, int32_t kind, const rt_tile_plan* plan,
+                       void* stream);
+
+/* Forward: replaces layers.py:83-94 (logits * scale, masked softmax, PV) for
+ * inputs already normalised (q_hat * tau, k_hat; layers.py:65-80).
+ *   q, k, v [batch][heads][seq_len][head_dim] bf16;  head_dim in {32, 64}
+ *   o       same shape, bf16
+ *   lse     [batch][heads][seq_len] fp32, natural-log sum of exp over live keys
+ * scale multiplies q.k (the reference divides by sqrt(head_dim)). */
+int rt_attention_fwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, int32_t batch,
+                     int32_t heads, int32_t seq_len, int32_t head_dim, float scale,
+                     const rt_tile_plan* plan, uint16_t* o, float* lse, void* stream);
+
+/* Workspace for the backward: [batch][heads][seq_len] fp32 (rowsum(dO * O)). */
+size_t rt_attention_bwd_workspace_bytes(int32_t batch, int32_t heads, int32_t seq_len);
+
+/* Backward: the gradients jax autodiff takes through layers.py:83-94.
+ *   d_o  [batch][heads][seq_len][head_dim] bf16 (upstream gradient of o)
+ *   o, lse as produced by rt_attention_fwd
+ *   dq, dk, dv  bf16, same shape as q (written, not accumulated) */
+int rt_attention_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* o,
+                     const uint16_t* d_o, const float* lse, int32_t batch, int32_t heads,
+                     int32_t seq_len, int32_t head_dim, float scale, const rt_tile_plan* plan,
+                     uint16_t* dq, uint16_t* dk, uint16_t* dv, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* Sticky device status (RT_OK or RT_ERR_TIMEOUT) raised by any kernel of the
+ * library on the current device. Synchronises the device. If `reset` is
+ * non-zero the status is cleared after reading. */
+int rt_device_status(int32_t reset);
+
+/* Static description of a status code. */
+const char* rt_status_string(int32_t status);
+
+/* Library ABI version (major * 100 + minor). */
+int32_t rt_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RT_ATTENTION_H */

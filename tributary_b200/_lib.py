@@ -1,0 +1,108 @@
+"""ctypes binding of libtributary_b200.so (the C ABI in include/rt_attention.h).
+
+This is the same binding a reference-side integration writes (see
+INTEGRATION.md); the Python host layer in ``tributary_b200.attention`` and the
+tests call the library through it. There is no fallback: if the shared
+library is missing or fails to load, ``load()`` raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+from .build import LIB_PATH
+
+RT_OK = 0
+RT_ERR_INVALID_ARGUMENT = 1
+RT_ERR_UNSUPPORTED = 2
+RT_ERR_CUDA = 3
+RT_ERR_TIMEOUT = 4
+RT_ERR_WORKSPACE = 5
+RT_ERR_DEVICE = 6
+
+RT_MASK_COLUMN = 0
+RT_MASK_FEATURE = 1
+RT_MASK_NEIGHBOR = 2
+RT_MASK_FULL = 3
+
+TILE = 128
+
+EXPORTED = (
+    "rt_tile_plan_bytes", "rt_tile_plan_bind", "rt_build_tile_plan",
+    "rt_attention_fwd", "rt_attention_bwd_workspace_bytes", "rt_attention_bwd",
+    "rt_device_status", "rt_status_string", "rt_version",
+)
+
+
+class RtTilePlan(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int32),
+        ("seq_len", ctypes.c_int32),
+        ("max_rows", ctypes.c_int32),
+        ("tiles", ctypes.c_int32),
+        ("words", ctypes.c_int32),
+        ("live_bits", ctypes.c_void_p),
+        ("full_bits", ctypes.c_void_p),
+        ("q2k_ptr", ctypes.c_void_p),
+        ("q2k_idx", ctypes.c_void_p),
+        ("k2q_ptr", ctypes.c_void_p),
+        ("k2q_idx", ctypes.c_void_p),
+        ("tile_masks", ctypes.c_void_p),
+        ("tile_masks_t", ctypes.c_void_p),
+        ("fk_bits", ctypes.c_void_p),
+        ("nnz", ctypes.c_void_p),
+    ]
+
+
+class RtError(RuntimeError):
+    def __init__(self, status: int, what: str, message: str):
+        super().__init__(f"{what}: {message} (status {status})")
+        self.status = status
+
+
+_LIB = None
+
+
+def _declare(lib):
+    vp, i32, f32, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_float, ctypes.c_size_t
+    plan_p = ctypes.POINTER(RtTilePlan)
+    lib.rt_tile_plan_bytes.argtypes = [i32, i32, i32]
+    lib.rt_tile_plan_bytes.restype = sz
+    lib.rt_tile_plan_bind.argtypes = [vp, sz, i32, i32, i32, plan_p]
+    lib.rt_tile_plan_bind.restype = ctypes.c_int
+    lib.rt_build_tile_plan.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, i32, plan_p, vp]
+    lib.rt_build_tile_plan.restype = ctypes.c_int
+    lib.rt_attention_fwd.argtypes = [vp, vp, vp, i32, i32, i32, i32, f32, plan_p, vp, vp, vp]
+    lib.rt_attention_fwd.restype = ctypes.c_int
+    lib.rt_attention_bwd_workspace_bytes.argtypes = [i32, i32, i32]
+    lib.rt_attention_bwd_workspace_bytes.restype = sz
+    lib.rt_attention_bwd.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, plan_p,
+                                     vp, vp, vp, vp, sz, vp]
+    lib.rt_attention_bwd.restype = ctypes.c_int
+    lib.rt_device_status.argtypes = [i32]
+    lib.rt_device_status.restype = ctypes.c_int
+    lib.rt_status_string.argtypes = [i32]
+    lib.rt_status_string.restype = ctypes.c_char_p
+    lib.rt_version.argtypes = []
+    lib.rt_version.restype = i32
+
+
+def load(path: str | None = None):
+    """Load (once) and return the ctypes handle of the CUDA library."""
+    global _LIB
+    if _LIB is not None and path is None:
+        return _LIB
+    p = path or LIB_PATH
+    if not os.path.exists(p):
+        raise RuntimeError(f"CUDA library not built: {p} (run python -m tributary_b200.build)")
+    lib = ctypes.CDLL(p)
+    _declare(lib)
+    if path is None:
+        _LIB = lib
+    return lib
+
+
+def check(status: int, what: str):
+    if status != RT_OK:
+        msg = load().rt_status_string(status).decode()
+        raise RtError(status, what, msg)

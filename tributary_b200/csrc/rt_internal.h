@@ -1,0 +1,27 @@
+// Internal declarations shared by the kernels and the C ABI (host side).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "rt_attention.h"
+
+namespace rt {
+
+int launch_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids, const int32_t* column_ids,
+                           const uint8_t* is_padding, const uint8_t* fk_adj, int B, int S, int R,
+                           int kind, const rt_tile_plan& plan, cudaStream_t stream);
+
+int launch_attention_fwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S,
+                         int Dh, float scale, const rt_tile_plan& plan, uint16_t* o, float* lse,
+                         cudaStream_t stream);
+
+int launch_attention_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* o,
+                         const uint16_t* d_o, const float* lse, int B, int H, int S, int Dh,
+                         float scale, const rt_tile_plan& plan, uint16_t* dq, uint16_t* dk,
+                         uint16_t* dv, float* delta, cudaStream_t stream);
+
+// TMA descriptor for a [rows_total][Dh] bf16 matrix viewed as (Dh, S, B*H),
+// box (Dh, 128, 1), 128B swizzle for Dh = 64, 64B swizzle for Dh = 32.
+int make_qkv_tensor_map(CUtensorMap* map, const void* base, int BH, int S, int Dh);
+
+}  // namespace rt

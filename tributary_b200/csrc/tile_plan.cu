@@ -1,0 +1,257 @@
+// Prepass: token metadata -> tile occupancy bitmaps, per-tile element bits
+// and compacted tile lists for one mask kind.
+//
+// Replaces build_attention_masks (confluence/confluence/model.py:201-264)
+// followed by the mask permutation of GatedAttentionSublayer
+// (confluence/confluence/layers.py:144-152). Instead of materialising
+// [B,S,S] masks, each 128x128 tile of the *permuted* mask is evaluated from
+// the token metadata (row id, column id, padding flag, fk adjacency bits)
+// and reduced to: live / fully-live flags, and -- for live tiles that are
+// not fully live -- its 128x128 element bits in both orientations (query-
+// major for the forward and dQ kernels, key-major for dK/dV). Fully-live
+// and dead tiles write no element bits; the attention kernels never read them.
+//
+// Element rule for permuted positions i, j (model.py:227-262):
+//   valid = !pad[p_i] && !pad[p_j]
+//   rel   = COLUMN:   col[p_i] == col[p_j]
+//           FEATURE:  row_i == row_j || fk_adj[row_i][row_j]
+//           NEIGHBOR: fk_adj[row_j][row_i]
+//           FULL:     true
+//   mask  = (rel && valid) || p_i == p_j
+// with p = min(perm[b][.], S-1) and row = min(seq_row_ids[b][p], R-1): indices
+// past the end clamp, as jax gathers do, so no input can read out of bounds.
+#include "rt_device.cuh"
+#include "rt_internal.h"
+
+namespace rt {
+
+// fk_bits[b][r][w] bit t = FEATURE: fk_adj[b][r][32w+t]; NEIGHBOR: fk_adj[b][32w+t][r]
+__global__ void fk_pack_kernel(const uint8_t* __restrict__ fk_adj, int R, int WR, int transpose,
+                               uint32_t* __restrict__ fk_bits) {
+  const int b = blockIdx.y;
+  const int r = blockIdx.x;
+  const uint8_t* base = fk_adj + (size_t)b * R * R;
+  for (int w = threadIdx.x; w < WR; w += blockDim.x) {
+    uint32_t word = 0;
+    for (int t = 0; t < 32; ++t) {
+      const int c = w * 32 + t;
+      if (c < R) {
+        const uint8_t v = transpose ? base[(size_t)c * R + r] : base[(size_t)r * R + c];
+        word |= (v != 0 ? 1u : 0u) << t;
+      }
+    }
+    fk_bits[((size_t)b * R + r) * WR + w] = word;
+  }
+}
+
+__global__ void __launch_bounds__(128) tile_mask_kernel(
+    const uint16_t* __restrict__ perm, const uint16_t* __restrict__ seq_row_ids,
+    const int32_t* __restrict__ column_ids, const uint8_t* __restrict__ is_padding,
+    const uint32_t* __restrict__ fk_bits, int S, int R, int WR, int kind, rt_tile_plan plan) {
+  const int kt = blockIdx.x;
+  const int qt = blockIdx.y;
+  const int b = blockIdx.z;
+  const int T = plan.tiles;
+  const int t = threadIdx.x;
+  const int lane = t & 31;
+  const int warp = t >> 5;
+
+  __shared__ int s_korig[RT_TILE];
+  __shared__ int s_krow[RT_TILE];
+  __shared__ int s_kcol[RT_TILE];
+  __shared__ unsigned char s_kpad[RT_TILE];
+
+  const size_t boff = (size_t)b * S;
+  {
+    const int j = kt * RT_TILE + t;
+    if (j < S) {
+      const int pj = min((int)perm[boff + j], S - 1);  // out-of-range perm entries clamp
+      int rj = seq_row_ids[boff + pj];
+      if (R > 0 && rj > R - 1) rj = R - 1;
+      s_korig[t] = pj;
+      s_krow[t] = rj;
+      s_kcol[t] = column_ids[boff + pj];
+      s_kpad[t] = is_padding[boff + pj] != 0;
+    } else {
+      s_korig[t] = -1;
+      s_krow[t] = 0;
+      s_kcol[t] = 0;
+      s_kpad[t] = 1;
+    }
+  }
+  const int i = qt * RT_TILE + t;
+  const bool qin = i < S;
+  int pi = -2, ri = 0, ci = 0;
+  bool padi = true;
+  if (qin) {
+    pi = min((int)perm[boff + i], S - 1);
+    ri = seq_row_ids[boff + pi];
+    if (R > 0 && ri > R - 1) ri = R - 1;
+    ci = column_ids[boff + pi];
+    padi = is_padding[boff + pi] != 0;
+  }
+  const uint32_t* fkrow = (R > 0 && fk_bits != nullptr) ? fk_bits + ((size_t)b * R + ri) * WR : nullptr;
+  __syncthreads();
+
+  uint32_t w4[4];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    uint32_t word = 0;
+    if (qin) {
+#pragma unroll 8
+      for (int u = 0; u < 32; ++u) {
+        const int j = w * 32 + u;
+        const int pj = s_korig[j];
+        bool m = false;
+        if (pj >= 0) {
+          const bool valid = !padi && !s_kpad[j];
+          bool rel;
+          if (kind == RT_MASK_COLUMN) {
+            rel = ci == s_kcol[j];
+          } else if (kind == RT_MASK_FEATURE) {
+            const int rj = s_krow[j];
+            rel = (ri == rj) || (fkrow != nullptr && ((__ldg(fkrow + (rj >> 5)) >> (rj & 31)) & 1u));
+          } else if (kind == RT_MASK_NEIGHBOR) {
+            const int rj = s_krow[j];
+            rel = fkrow != nullptr && ((__ldg(fkrow + (rj >> 5)) >> (rj & 31)) & 1u);
+          } else {
+            rel = true;
+          }
+          m = (rel && valid) || (pi == pj);
+        }
+        word |= (m ? 1u : 0u) << u;
+      }
+    }
+    w4[w] = word;
+  }
+
+  const int any = __syncthreads_or((w4[0] | w4[1] | w4[2] | w4[3]) != 0u);
+  const int all = __syncthreads_and(qin && (w4[0] & w4[1] & w4[2] & w4[3]) == 0xFFFFFFFFu);
+  if (!any) return;  // block-uniform
+  const size_t tile_q = ((size_t)b * T + qt) * T + kt;
+  const size_t tile_k = ((size_t)b * T + kt) * T + qt;
+  if (t == 0) {
+    const size_t wi = ((size_t)b * T + qt) * plan.words + (kt >> 5);
+    atomicOr(plan.live_bits + wi, 1u << (kt & 31));
+    if (all) atomicOr(plan.full_bits + wi, 1u << (kt & 31));
+  }
+  if (all) return;  // block-uniform
+  reinterpret_cast<uint4*>(plan.tile_masks)[tile_q * RT_TILE + t] =
+      make_uint4(w4[0], w4[1], w4[2], w4[3]);
+  // Transpose 128x128 bits: for key j, this warp's 32 queries form word `warp`
+  // of key j's row in the key-major copy.
+  uint32_t tw[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+#pragma unroll 8
+    for (int u = 0; u < 32; ++u) {
+      const uint32_t bal = __ballot_sync(0xFFFFFFFFu, (w4[w] >> u) & 1u);
+      if (lane == u) tw[w] = bal;
+    }
+  }
+  uint32_t* dst = plan.tile_masks_t + tile_k * RT_TILE * 4;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) dst[(size_t)(w * 32 + lane) * 4 + warp] = tw[w];
+}
+
+// Single block: CSR lists (q2k over (b,qt) rows, k2q over (b,kt) rows) from the bitmaps.
+__global__ void __launch_bounds__(1024) tile_list_kernel(rt_tile_plan plan) {
+  const int T = plan.tiles;
+  const int W = plan.words;
+  const int nrows = plan.batch * T;
+  const int nthreads = blockDim.x;
+  const int chunk = (nrows + nthreads - 1) / nthreads;
+  const int r0 = min(nrows, (int)threadIdx.x * chunk);
+  const int r1 = min(nrows, r0 + chunk);
+  __shared__ int s_warp[32];
+  __shared__ int s_total;
+
+  for (int pass = 0; pass < 2; ++pass) {
+    const bool by_q = pass == 0;
+    int* ptr = by_q ? plan.q2k_ptr : plan.k2q_ptr;
+    int* idx = by_q ? plan.q2k_idx : plan.k2q_idx;
+    int local = 0;
+    for (int r = r0; r < r1; ++r) {
+      const int b = r / T, x = r % T;
+      if (by_q) {
+        for (int w = 0; w < W; ++w) local += __popc(plan.live_bits[((size_t)b * T + x) * W + w]);
+      } else {
+        for (int q = 0; q < T; ++q)
+          local += (plan.live_bits[((size_t)b * T + q) * W + (x >> 5)] >> (x & 31)) & 1u;
+      }
+    }
+    // exclusive block scan of `local`
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      const int nw = (nthreads + 31) >> 5;
+      int v = lane < nw ? s_warp[lane] : 0;
+      int vi = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xFFFFFFFFu, vi, o);
+        if (lane >= o) vi += u;
+      }
+      if (lane < nw) s_warp[lane] = vi - v;
+      if (lane == 31) s_total = vi;
+    }
+    __syncthreads();
+    int pos = s_warp[warp] + incl - local;
+    for (int r = r0; r < r1; ++r) {
+      const int b = r / T, x = r % T;
+      ptr[r] = pos;
+      if (by_q) {
+        for (int kt = 0; kt < T; ++kt) {
+          const size_t wi = ((size_t)b * T + x) * W + (kt >> 5);
+          if ((plan.live_bits[wi] >> (kt & 31)) & 1u) {
+            const bool full = (plan.full_bits[wi] >> (kt & 31)) & 1u;
+            idx[pos++] = kt | (full ? (int)0x80000000u : 0);
+          }
+        }
+      } else {
+        for (int qt = 0; qt < T; ++qt) {
+          const size_t wi = ((size_t)b * T + qt) * W + (x >> 5);
+          if ((plan.live_bits[wi] >> (x & 31)) & 1u) {
+            const bool full = (plan.full_bits[wi] >> (x & 31)) & 1u;
+            idx[pos++] = qt | (full ? (int)0x80000000u : 0);
+          }
+        }
+      }
+    }
+    if (threadIdx.x == 0) {
+      ptr[nrows] = s_total;
+      if (by_q) *plan.nnz = s_total;
+    }
+    __syncthreads();
+  }
+}
+
+int launch_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids, const int32_t* column_ids,
+                           const uint8_t* is_padding, const uint8_t* fk_adj, int B, int S, int R,
+                           int kind, const rt_tile_plan& plan, cudaStream_t stream) {
+  const int T = plan.tiles;
+  const int W = plan.words;
+  const int WR = (R + 31) / 32;
+  if (cudaMemsetAsync(plan.live_bits, 0, sizeof(uint32_t) * (size_t)B * T * W, stream) != cudaSuccess ||
+      cudaMemsetAsync(plan.full_bits, 0, sizeof(uint32_t) * (size_t)B * T * W, stream) != cudaSuccess)
+    return RT_ERR_CUDA;
+  const uint32_t* fk_bits = nullptr;
+  if ((kind == RT_MASK_FEATURE || kind == RT_MASK_NEIGHBOR) && R > 0) {
+    fk_pack_kernel<<<dim3(R, B), 32, 0, stream>>>(fk_adj, R, WR, kind == RT_MASK_NEIGHBOR ? 1 : 0,
+                                                  plan.fk_bits);
+    fk_bits = plan.fk_bits;
+  }
+  tile_mask_kernel<<<dim3(T, T, B), RT_TILE, 0, stream>>>(perm, seq_row_ids, column_ids, is_padding,
+                                                           fk_bits, S, R, WR, kind, plan);
+  tile_list_kernel<<<1, 1024, 0, stream>>>(plan);
+  return cudaGetLastError() == cudaSuccess ? RT_OK : RT_ERR_CUDA;
+}
+
+}  // namespace rt
