@@ -1,0 +1,462 @@
+"""Benchmark: RT masked attention fwd+bwd on B200 (cells/s, live-tile TFLOP/s).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c|b] [--impl ours|reference]
+
+One step = for each mask kind (column, feature, neighbor, full): the
+tile-plan prepass from the batch's token metadata, the forward and the
+backward attention kernels, all through the library's C ABI. Inputs (token
+metadata and q/k/v/dO for every kind, > 1 GB for the default workload) are
+resident in HBM, larger than L2, and distinct per kind. Under torchrun each
+rank runs the same workload on its own batch (weak scaling, no collective in
+the data path); the time is the max over ranks.
+
+``--impl reference`` times the CPU restatement of the reference math
+(numpy fp32 dense masked attention + analytic backward, multithreaded BLAS)
+on a bounded sample of the same workload on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+KIND_NAMES = ("column", "feature", "neighbor", "full")
+
+# Workloads (benchmark configurations of the RT attention path)
+CONFIGS = {
+    # B=8, S=4096, 16 heads x 64; generator tuned for a spread of tile densities
+    "c": dict(name="rt_attn_fwd_bwd_b8_s4096_h16_d64", B=8, S=4096, H=16, Dh=64,
+              tables=24, cells_lo=4, cells_hi=16, p_fk=0.9, max_parents=2, pad=0.05),
+    # B=32, S=1024, 8 heads x 32; 6 tables, 4-16 cells, p_fk 0.7, 10% padding
+    "b": dict(name="rt_attn_fwd_bwd_b32_s1024_h8_d32", B=32, S=1024, H=8, Dh=32,
+              tables=6, cells_lo=4, cells_hi=16, p_fk=0.7, max_parents=1, pad=0.10),
+}
+
+FLOPS_PER_LIVE_TILE = {"fwd": 4, "bwd": 10}  # x 128^2 x Dh per live (b, h, tile pair)
+
+
+def measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, 6650.0, "fallback"
+
+
+def make_metadata(cfg, seed):
+    from oracle import rt_oracle as orc  # workload generator only (seeded synthetic batch)
+    return orc.make_batch(seed, cfg["B"], cfg["S"], cfg["tables"], cfg["cells_lo"], cfg["cells_hi"],
+                          cfg["p_fk"], cfg["pad"], max_parents=cfg["max_parents"])
+
+
+def perm_for(bt, kind):
+    if kind == 0:
+        return bt["col_perm"]
+    if kind == 1:
+        return bt["out_perm"]
+    if kind == 2:
+        return bt["in_perm"]
+    b, s = bt["seq_row_ids"].shape
+    return np.broadcast_to(np.arange(s, dtype=np.uint16), (b, s)).copy()
+
+
+# ----------------------------------------------------------------------------
+# clocks sampling (nvidia-smi during the timed region)
+# ----------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.device_index = device_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"rt_bench_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax = float(parts[2])
+                except ValueError:
+                    continue
+                for name, val in zip(names, parts[5:9]):
+                    if val.lower().startswith("active"):
+                        reasons.add(name)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------
+# our arm
+# ----------------------------------------------------------------------------
+class Workload:
+    """Device-resident inputs, plans and outputs for one rank."""
+
+    def __init__(self, cfg, seed, device):
+        import torch
+        from tributary_b200 import attention as rt
+        self.cfg = cfg
+        self.rt = rt
+        self.torch = torch
+        B, S, H, Dh = cfg["B"], cfg["S"], cfg["H"], cfg["Dh"]
+        bt = make_metadata(cfg, seed)
+        self.meta_host = bt
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        self.kinds = []
+        for kind in range(4):
+            perm = torch.from_numpy(np.ascontiguousarray(perm_for(bt, kind)).view(np.int16))
+            host = {
+                "perm": perm,
+                "seq_row_ids": torch.from_numpy(bt["seq_row_ids"].view(np.int16)),
+                "column_ids": torch.from_numpy(bt["column_ids"]),
+                "is_padding": torch.from_numpy(bt["is_padding"]),
+                "fk_adj": torch.from_numpy(bt["fk_adj"]),
+            }
+            # q_hat, k_hat unit vectors (tau = sqrt(Dh) folded into q), v, dO ~ N(0,1)
+            q = torch.randn(B, H, S, Dh, generator=g)
+            k = torch.randn(B, H, S, Dh, generator=g)
+            q = q / q.norm(dim=-1, keepdim=True) * math.sqrt(Dh)
+            k = k / k.norm(dim=-1, keepdim=True)
+            v = torch.randn(B, H, S, Dh, generator=g)
+            do = torch.randn(B, H, S, Dh, generator=g)
+            for name, t in (("q", q), ("k", k), ("v", v), ("do", do)):
+                host[name] = t.to(torch.bfloat16)
+            dev = {n: t.to(device) for n, t in host.items()}
+            plan = rt.build_tile_plan(dev["perm"], dev["seq_row_ids"], dev["column_ids"],
+                                      dev["is_padding"], dev["fk_adj"], kind)
+            o = torch.empty_like(dev["q"])
+            lse = torch.empty(B, H, S, dtype=torch.float32, device=device)
+            grads = [torch.empty_like(dev["q"]) for _ in range(3)]
+            ws = torch.empty(rt._lib.load().rt_attention_bwd_workspace_bytes(B, H, S),
+                             dtype=torch.uint8, device=device)
+            pinned = {n: t.pin_memory() for n, t in host.items()}
+            out_pinned = [torch.empty_like(host["q"]).pin_memory() for _ in range(4)]
+            self.kinds.append(dict(kind=kind, dev=dev, plan=plan, o=o, lse=lse, grads=grads, ws=ws,
+                                   pinned=pinned, out_pinned=out_pinned))
+        torch.cuda.synchronize()
+        self.nnz = [k["plan"].nnz() for k in self.kinds]
+        self.tiles = self.kinds[0]["plan"].tiles
+
+    def launches_per_step(self):
+        # prepass: fk pack (feature / neighbor only), tile mask, tile list;
+        # forward: 1; backward: row stats, dK/dV, dQ
+        return sum((3 if k in (1, 2) else 2) + 1 + 3 for k in range(4))
+
+    def rebuild_plan(self, k):
+        lib = self.rt._lib
+        d = k["dev"]
+        B, S = self.cfg["B"], self.cfg["S"]
+        R = d["fk_adj"].shape[1]
+        lib.check(lib.load().rt_build_tile_plan(
+            d["perm"].data_ptr(), d["seq_row_ids"].data_ptr(), d["column_ids"].data_ptr(),
+            d["is_padding"].data_ptr(), d["fk_adj"].data_ptr(), B, S, R, k["kind"],
+            self.rt.ctypes.byref(k["plan"].c), self.torch.cuda.current_stream().cuda_stream),
+            "rt_build_tile_plan")
+
+    def step(self, events=None):
+        rt = self.rt
+        scale = 1.0 / math.sqrt(self.cfg["Dh"])
+        for k in self.kinds:
+            d = k["dev"]
+            if events is not None:
+                events["plan"][0].record()
+            self.rebuild_plan(k)
+            if events is not None:
+                events["plan"][1].record()
+                events["fwd"][0].record()
+            rt.attention_fwd(d["q"], d["k"], d["v"], k["plan"], scale, out=k["o"], lse=k["lse"])
+            if events is not None:
+                events["fwd"][1].record()
+                events["bwd"][0].record()
+            rt.attention_bwd(d["q"], d["k"], d["v"], k["o"], k["lse"], d["do"], k["plan"], scale,
+                             dq=k["grads"][0], dk=k["grads"][1], dv=k["grads"][2], workspace=k["ws"])
+            if events is not None:
+                events["bwd"][1].record()
+                for name in ("plan", "fwd", "bwd"):
+                    events["acc"][name].append((events[name][0], events[name][1]))
+                    events[name] = (self.torch.cuda.Event(enable_timing=True),
+                                    self.torch.cuda.Event(enable_timing=True))
+
+    def step_e2e(self):
+        """Same pass through the public API with host buffers: pinned host ->
+        device copies of every input, then o, dq, dk, dv back to the host."""
+        rt = self.rt
+        scale = 1.0 / math.sqrt(self.cfg["Dh"])
+        h2d = d2h = 0
+        for k in self.kinds:
+            d, p = k["dev"], k["pinned"]
+            for n in ("perm", "seq_row_ids", "column_ids", "is_padding", "fk_adj", "q", "k", "v", "do"):
+                d[n].copy_(p[n], non_blocking=True)
+                h2d += p[n].numel() * p[n].element_size()
+            self.rebuild_plan(k)
+            rt.attention_fwd(d["q"], d["k"], d["v"], k["plan"], scale, out=k["o"], lse=k["lse"])
+            rt.attention_bwd(d["q"], d["k"], d["v"], k["o"], k["lse"], d["do"], k["plan"], scale,
+                             dq=k["grads"][0], dk=k["grads"][1], dv=k["grads"][2], workspace=k["ws"])
+            for dst, src in zip(k["out_pinned"], [k["o"]] + k["grads"]):
+                dst.copy_(src, non_blocking=True)
+                d2h += src.numel() * src.element_size()
+        return h2d, d2h
+
+    def live_tile_flops(self):
+        """Algorithmic FLOPs of one step (fwd 4, bwd 10 x 128^2 x Dh per live tile-head)."""
+        h, dh = self.cfg["H"], self.cfg["Dh"]
+        per = {"fwd": 0, "bwd": 0}
+        for nnz in self.nnz:
+            for p in per:
+                per[p] += FLOPS_PER_LIVE_TILE[p] * 128 * 128 * dh * h * nnz
+        return per
+
+    def algorithmic_bytes(self):
+        b, s, h, dh = (self.cfg[x] for x in ("B", "S", "H", "Dh"))
+        fwd = 8 * b * h * s * dh + 4 * b * h * s
+        bwd = 16 * b * h * s * dh + 8 * b * h * s
+        return {"fwd": 4 * fwd, "bwd": 4 * bwd}
+
+
+def dist_setup(n_gpus):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    import torch
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def cpu_sample(cfg, seed, budget_s=15.0, threads=None):
+    """Time the numpy restatement (fp32 dense masked attention fwd + analytic
+    bwd) on a bounded sample: batch element 0, `hs` heads, each mask kind.
+    Returns (cells_per_s, sample description, threads used)."""
+    from oracle import rt_oracle as orc  # CPU baseline leg
+    bt = make_metadata(dict(cfg, B=1), seed)
+    S, H, Dh = cfg["S"], cfg["H"], cfg["Dh"]
+    rng = np.random.default_rng(seed)
+    hs = 2 if S >= 4096 else min(H, 4)
+    q, k, v, do = (rng.standard_normal((1, hs, S, Dh)).astype(np.float32) for _ in range(4))
+    scale = np.float32(1.0 / math.sqrt(Dh))
+    masks = []
+    for kind in range(4):
+        m = orc.mask_for_kind(kind, bt["seq_row_ids"], bt["fk_adj"], bt["column_ids"], bt["is_padding"])
+        masks.append(orc.permute_mask(m, perm_for(bt, kind)))
+    t0 = time.perf_counter()
+    calls = 0
+    while True:
+        for kind in range(4):
+            o, lse = orc.attention_fwd(q, k, v, masks[kind], scale)
+            orc.attention_bwd(q, k, v, o, do, masks[kind], scale)
+            calls += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    cells = calls * S * hs / H  # a call over all H heads counts S cells
+    return cells / dt, f"b=1 of {cfg['B']}, {hs} of {H} heads, {calls} fwd+bwd calls over the 4 kinds", threads
+
+
+def run_reference_arm(args, cfg):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cores = len(os.sched_getaffinity(0))
+    values = []
+    per_step = max(1.0, min(8.0, 150.0 / max(1, args.steps)))
+    for _ in range(args.warmup):
+        cpu_sample(cfg, 1234, budget_s=1.0)
+    for _ in range(args.steps):
+        v, sample, _ = cpu_sample(cfg, 1234, budget_s=per_step)
+        values.append(v)
+    value = statistics.median(values)
+    ms_per_step = 1e3 * 4 * cfg["B"] * cfg["S"] / value
+    line = {
+        "impl": "reference", "metric": "rt_attention_fwd_bwd_cells_per_s", "value": value,
+        "unit": "cells/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": cfg["name"], "B": cfg["B"], "S": cfg["S"], "H": cfg["H"], "Dh": cfg["Dh"],
+                   "masks": list(KIND_NAMES)},
+        "cpu_baseline": {"value": value, "unit": "cells/s", "cores": cores, "kind": "port",
+                         "sample": sample + "; numpy fp32 restatement of the reference path "
+                                   "(jax/XLA-CPU not installable)"},
+        "e2e": {"value": value, "unit": "cells/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_our_arm(args, cfg):
+    import torch
+    world, rank, local = dist_setup(args.gpus)
+    wl = Workload(cfg, seed=1000 + rank, device=torch.device("cuda", local))
+    from tributary_b200.attention import device_status
+
+    for _ in range(args.warmup):
+        wl.step()
+    barrier(world)
+    if device_status(reset=True) != 0:
+        raise RuntimeError("device status error during warm-up")
+
+    # ---- timed region: K steps, device time by events, max over ranks ----
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    barrier(world)
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    for _ in range(args.steps):
+        wl.step()
+    t_end.record()
+    barrier(world)
+    step_ms = t_start.elapsed_time(t_end) / args.steps
+    # per-entry-point breakdown over the same number of steps
+    ev = {n: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for n in ("plan", "fwd", "bwd")}
+    ev["acc"] = {"plan": [], "fwd": [], "bwd": []}
+    for _ in range(args.steps):
+        wl.step(events=ev)
+    barrier(world)
+    clocks = sampler.stop()
+    part_ms = {n: sum(a.elapsed_time(b) for a, b in ev["acc"][n]) / args.steps for n in ("plan", "fwd", "bwd")}
+    step_ms = max_over_ranks(step_ms, world)
+    part_ms = {n: max_over_ranks(v, world) for n, v in part_ms.items()}
+
+    # ---- end to end through the public API with host buffers ----
+    for _ in range(2):
+        wl.step_e2e()
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        h2d, d2h = wl.step_e2e()
+    e1.record()
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    status = device_status(reset=True)
+    if status != 0:
+        raise RuntimeError(f"device status error {status}")
+
+    cfgd = wl.cfg
+    cells_step = 4 * cfgd["B"] * cfgd["S"]  # 4 attention calls (one per mask kind) per step
+    value = world * cells_step / (step_ms * 1e-3)
+    flops = wl.live_tile_flops()
+    peak_tf, peak_gbs, peak_src = measured_peaks()
+    attn_ms = part_ms["fwd"] + part_ms["bwd"]
+    achieved_tf = (flops["fwd"] + flops["bwd"]) / (attn_ms * 1e-3) / 1e12
+    densities = {KIND_NAMES[i]: wl.nnz[i] / (cfgd["B"] * wl.tiles * wl.tiles) for i in range(4)}
+    if rank == 0:
+        line = {
+            "metric": "rt_attention_fwd_bwd_cells_per_s", "value": value, "unit": "cells/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": cfgd["name"], "B": cfgd["B"], "S": cfgd["S"], "H": cfgd["H"],
+                       "Dh": cfgd["Dh"], "masks": list(KIND_NAMES),
+                       "generator": {k: cfgd[k] for k in ("tables", "cells_lo", "cells_hi", "p_fk",
+                                                          "max_parents", "pad")},
+                       "live_tile_density": densities,
+                       "l2": "inputs > L2 (q/k/v/dO distinct per kind, %.2f GB resident)" % (
+                           16 * cfgd["B"] * cfgd["H"] * cfgd["S"] * cfgd["Dh"] * 2 / 1e9),
+                       "parallelism": f"batch-sharded x{world} (replicas, no collective)"},
+            "tflops_live_tiles": achieved_tf,
+            "frac_of_bf16_peak": achieved_tf / peak_tf,
+            "breakdown_ms_per_step": part_ms,
+            "roofline": {"bound": "tensor", "kernel": "attention fwd+bwd (attn_fwd, row_stats, dkdv, dq)",
+                         "achieved": achieved_tf, "peak": peak_tf, "unit": "TFLOP/s",
+                         "frac": achieved_tf / peak_tf, "peak_source": peak_src + " bf16 dense (burst)",
+                         "traffic": None},
+            "e2e": {"value": world * cells_step / (e2e_ms * 1e-3), "unit": "cells/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": wl.launches_per_step() * args.steps,
+            "clocks": clocks,
+        }
+        if not args.no_cpu_baseline:
+            v, sample, _ = cpu_sample(cfgd, 1234, budget_s=args.cpu_seconds)
+            line["cpu_baseline"] = {"value": v, "unit": "cells/s", "cores": len(os.sched_getaffinity(0)),
+                                    "kind": "port", "sample": sample}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference_arm(args, cfg)
+    else:
+        run_our_arm(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

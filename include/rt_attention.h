@@ -113,7 +113,8 @@ int rt_attention_fwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, in
                      int32_t heads, int32_t seq_len, int32_t head_dim, float scale,
                      const rt_tile_plan* plan, uint16_t* o, float* lse, void* stream);
 
-/* Workspace for the backward: [batch][heads][seq_len] fp32 (rowsum(dO * O)). */
+/* Workspace for the backward: [batch*heads][2][seq_len rounded up to 128]
+ * fp32 -- lse (log2 units) and rowsum(dO * O) per query, zero past seq_len. */
 size_t rt_attention_bwd_workspace_bytes(int32_t batch, int32_t heads, int32_t seq_len);
 
 /* Backward: the gradients jax autodiff takes through layers.py:83-94.
@@ -133,6 +134,10 @@ int rt_device_status(int32_t reset);
 
 /* Static description of a status code. */
 const char* rt_status_string(int32_t status);
+
+/* Human-readable detail of the last RT_ERR_CUDA returned on the calling
+ * thread (the failing CUDA call and its error name); "" if none. */
+const char* rt_last_error(void);
 
 /* Library ABI version (major * 100 + minor). */
 int32_t rt_version(void);

@@ -374,16 +374,17 @@ def compute_rcm_perm(fk_adj, seq_row_ids, is_padding, outbound):
 # ----------------------------------------------------------------------------
 
 def make_batch(seed, B, S, n_tables, cells_lo, cells_hi, p_fk, pad_frac,
-               parent_window=None, R=None):
+               parent_window=None, R=None, max_parents=1):
     """Seeded synthetic sampler batch in the headwater layout.
 
     Each table t has a fixed width w_t ~ U[cells_lo, cells_hi] and global
     column ids base_t + 0..w_t-1 (column ids are global in the reference,
     documentation/model_architecture/batch_structure.md:46-47). Rows are
-    emitted in order with a uniformly drawn table; with probability p_fk a row
-    gets one FK parent among the earlier rows of the sample (the most recent
-    ``parent_window`` rows when given, else all of them), recorded as
-    fk_adj[b, child, parent] = 1 (sampler.rs:516-526). Cells past
+    emitted in order with a uniformly drawn table; a row draws up to
+    ``max_parents`` FK parents, each present with probability p_fk, among the
+    earlier rows of the sample (the most recent ``parent_window`` rows when
+    given, else all of them), recorded as fk_adj[b, child, parent] = 1
+    (sampler.rs:516-526; a row may have several FK parents). Cells past
     S*(1-pad_frac) are trailing padding (seq_row_id 0, column id 0, as the
     sampler leaves them, sampler.rs:336-347). R defaults to the largest row
     count in the batch.
@@ -402,15 +403,16 @@ def make_batch(seed, B, S, n_tables, cells_lo, cells_hi, p_fk, pad_frac,
         while pos < n_valid:
             t = int(rng.integers(n_tables))
             r = len(par)
-            parent = -1
-            if r > 0 and rng.random() < p_fk:
-                lo = 0 if parent_window is None else max(0, r - parent_window)
-                parent = int(rng.integers(lo, r))
+            ps = []
+            for _ in range(max_parents):
+                if r > 0 and rng.random() < p_fk:
+                    lo = 0 if parent_window is None else max(0, r - parent_window)
+                    ps.append(int(rng.integers(lo, r)))
             w = int(min(widths[t], n_valid - pos))
             column_ids[b, pos:pos + w] = bases[t] + np.arange(w)
             seq_row_ids[b, pos:pos + w] = r
             is_padding[b, pos:pos + w] = 0
-            par.append(parent)
+            par.append(ps)
             pos += w
         parents.append(par)
     max_r = max(1, max(len(p) for p in parents))
@@ -420,8 +422,8 @@ def make_batch(seed, B, S, n_tables, cells_lo, cells_hi, p_fk, pad_frac,
         raise ValueError(f"R={R} smaller than the {max_r} rows drawn")
     fk_adj = np.zeros((B, R, R), dtype=np.uint8)
     for b, par in enumerate(parents):
-        for child, parent in enumerate(par):
-            if parent >= 0:
+        for child, ps in enumerate(par):
+            for parent in ps:
                 fk_adj[b, child, parent] = 1
     col_perm = np.stack([compute_col_perm(column_ids[b], is_padding[b]) for b in range(B)])
     out_perm = np.stack([compute_rcm_perm(fk_adj[b], seq_row_ids[b], is_padding[b], True)

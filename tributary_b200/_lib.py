@@ -30,7 +30,7 @@ TILE = 128
 EXPORTED = (
     "rt_tile_plan_bytes", "rt_tile_plan_bind", "rt_build_tile_plan",
     "rt_attention_fwd", "rt_attention_bwd_workspace_bytes", "rt_attention_bwd",
-    "rt_device_status", "rt_status_string", "rt_version",
+    "rt_device_status", "rt_status_string", "rt_last_error", "rt_version",
 )
 
 
@@ -83,6 +83,8 @@ def _declare(lib):
     lib.rt_device_status.restype = ctypes.c_int
     lib.rt_status_string.argtypes = [i32]
     lib.rt_status_string.restype = ctypes.c_char_p
+    lib.rt_last_error.argtypes = []
+    lib.rt_last_error.restype = ctypes.c_char_p
     lib.rt_version.argtypes = []
     lib.rt_version.restype = i32
 
@@ -104,5 +106,8 @@ def load(path: str | None = None):
 
 def check(status: int, what: str):
     if status != RT_OK:
-        msg = load().rt_status_string(status).decode()
+        lib = load()
+        msg = lib.rt_status_string(status).decode()
+        if status == RT_ERR_CUDA:
+            msg += " -- " + lib.rt_last_error().decode()
         raise RtError(status, what, msg)

@@ -1,5 +1,6 @@
 // C ABI of the library: argument validation, plan layout, TMA descriptors and
 // launches. See include/rt_attention.h for the contract of each entry point.
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 
@@ -7,6 +8,22 @@
 #include "rt_internal.h"
 
 namespace rt {
+
+namespace {
+thread_local char g_last_error[256] = "";
+}
+
+int cuda_failure(cudaError_t err, const char* site) {
+  snprintf(g_last_error, sizeof(g_last_error), "%s: %s (%s)", site, cudaGetErrorName(err),
+           cudaGetErrorString(err));
+  return RT_ERR_CUDA;
+}
+
+int driver_failure(int err, const char* site) {
+  snprintf(g_last_error, sizeof(g_last_error), "%s: CUresult %d", site, err);
+  return RT_ERR_CUDA;
+}
+
 namespace {
 
 constexpr size_t kAlign = 256;
@@ -61,6 +78,44 @@ int check_device() {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Makes the device that owns `ptr` current for the duration of an entry point,
+// so that calls from threads with no current CUDA context (a framework's
+// worker threads) and with another device current both work. A different
+// previous device is restored on exit.
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(const void* ptr) {
+    cudaPointerAttributes attr;
+    cudaError_t e = cudaPointerGetAttributes(&attr, ptr);
+    if (e != cudaSuccess) {
+      status_ = cuda_failure(e, "cudaPointerGetAttributes");
+      return;
+    }
+    if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged) {
+      status_ = RT_ERR_INVALID_ARGUMENT;
+      return;
+    }
+    int cur = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess) cur = -1;
+    // cudaSetDevice also makes the device's primary context current on this thread.
+    e = cudaSetDevice(attr.device);
+    if (e != cudaSuccess) {
+      status_ = cuda_failure(e, "cudaSetDevice");
+      return;
+    }
+    if (cur >= 0 && cur != attr.device) restore_ = cur;
+    status_ = check_device();
+  }
+  ~DeviceGuard() {
+    if (restore_ >= 0) cudaSetDevice(restore_);
+  }
+  int status() const { return status_; }
+
+ private:
+  int status_ = RT_OK;
+  int restore_ = -1;
+};
+
 bool plan_matches(const rt_tile_plan* plan, int B, int S) {
   return plan != nullptr && plan->batch == B && plan->seq_len == S &&
          plan->tiles == (S + RT_TILE - 1) / RT_TILE && plan->live_bits && plan->full_bits &&
@@ -90,7 +145,7 @@ EncodeTiledFn encode_fn() {
 
 int make_qkv_tensor_map(CUtensorMap* map, const void* base, int BH, int S, int Dh) {
   EncodeTiledFn fn = encode_fn();
-  if (!fn) return RT_ERR_CUDA;
+  if (!fn) return driver_failure(-1, "cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)");
   cuuint64_t dims[3] = {(cuuint64_t)Dh, (cuuint64_t)S, (cuuint64_t)BH};
   cuuint64_t strides[2] = {(cuuint64_t)Dh * 2, (cuuint64_t)Dh * 2 * (cuuint64_t)S};
   cuuint32_t box[3] = {(cuuint32_t)Dh, (cuuint32_t)RT_TILE, 1};
@@ -99,7 +154,7 @@ int make_qkv_tensor_map(CUtensorMap* map, const void* base, int BH, int S, int D
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? RT_OK : RT_ERR_CUDA;
+  return r == CUDA_SUCCESS ? RT_OK : driver_failure((int)r, "cuTensorMapEncodeTiled");
 }
 
 }  // namespace rt
@@ -161,8 +216,8 @@ int rt_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids, const 
   if (!perm || !seq_row_ids || !column_ids || !is_padding) return RT_ERR_INVALID_ARGUMENT;
   const bool needs_fk = (kind == RT_MASK_FEATURE || kind == RT_MASK_NEIGHBOR) && max_rows > 0;
   if (needs_fk && (!fk_adj || !plan->fk_bits)) return RT_ERR_INVALID_ARGUMENT;
-  const int dev = check_device();
-  if (dev != RT_OK) return dev;
+  DeviceGuard guard(perm);
+  if (guard.status() != RT_OK) return guard.status();
   return launch_build_tile_plan(perm, seq_row_ids, column_ids, is_padding, fk_adj, batch, seq_len,
                                 max_rows, kind, *plan, static_cast<cudaStream_t>(stream));
 }
@@ -178,15 +233,16 @@ int rt_attention_fwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, in
   if (!q || !k || !v || !o || !lse) return RT_ERR_INVALID_ARGUMENT;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(lse))
     return RT_ERR_INVALID_ARGUMENT;
-  const int dev = check_device();
-  if (dev != RT_OK) return dev;
+  DeviceGuard guard(q);
+  if (guard.status() != RT_OK) return guard.status();
   return launch_attention_fwd(q, k, v, batch, heads, seq_len, head_dim, scale, *plan, o, lse,
                               static_cast<cudaStream_t>(stream));
 }
 
 size_t rt_attention_bwd_workspace_bytes(int32_t batch, int32_t heads, int32_t seq_len) {
   if (batch < 0 || heads < 0 || seq_len < 0) return 0;
-  return align_up(sizeof(float) * (size_t)batch * heads * seq_len);
+  const size_t padded = (size_t)((seq_len + RT_TILE - 1) / RT_TILE) * RT_TILE;
+  return align_up(2 * sizeof(float) * (size_t)batch * heads * padded);
 }
 
 int rt_attention_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* o,
@@ -205,19 +261,22 @@ int rt_attention_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, co
   for (const void* p : ptrs)
     if (!aligned16(p)) return RT_ERR_INVALID_ARGUMENT;
   if (workspace_bytes < rt_attention_bwd_workspace_bytes(batch, heads, seq_len)) return RT_ERR_WORKSPACE;
-  const int dev = check_device();
-  if (dev != RT_OK) return dev;
+  DeviceGuard guard(q);
+  if (guard.status() != RT_OK) return guard.status();
   return launch_attention_bwd(q, k, v, o, d_o, lse, batch, heads, seq_len, head_dim, scale, *plan, dq,
                               dk, dv, static_cast<float*>(workspace), static_cast<cudaStream_t>(stream));
 }
 
 int rt_device_status(int32_t reset) {
   int status = 0;
-  if (cudaDeviceSynchronize() != cudaSuccess) return RT_ERR_CUDA;
-  if (cudaMemcpyFromSymbol(&status, g_device_status, sizeof(int)) != cudaSuccess) return RT_ERR_CUDA;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_failure(e, "cudaDeviceSynchronize");
+  e = cudaMemcpyFromSymbol(&status, g_device_status, sizeof(int));
+  if (e != cudaSuccess) return cuda_failure(e, "cudaMemcpyFromSymbol(status)");
   if (reset) {
     const int zero = 0;
-    if (cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)) != cudaSuccess) return RT_ERR_CUDA;
+    e = cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return cuda_failure(e, "cudaMemcpyToSymbol(status)");
   }
   return status;
 }
@@ -236,5 +295,7 @@ const char* rt_status_string(int32_t status) {
 }
 
 int32_t rt_version(void) { return 100; }
+
+const char* rt_last_error(void) { return g_last_error; }
 
 }  // extern "C"

@@ -2,7 +2,7 @@
 // through confluence/confluence/layers.py:83-94 (the reference has no
 // hand-written backward; train.py:209 differentiates the forward).
 //
-//   delta_i = sum_d dO_id O_id                         (delta_kernel)
+//   delta_i = sum_d dO_id O_id                         (row_stats_kernel)
 //   p_ij    = mask_ij ? exp(s_ij - lse_i) : 0,  s = scale q k^T
 //   dP      = dO V^T ; dS = P o (dP - delta)
 //   dQ      = scale * dS K                             (dq_kernel: thread = query)
@@ -11,7 +11,7 @@
 // Both gradient kernels recompute P from lse, iterate only live tiles (q2k
 // list for dQ, k2q list for dK/dV) and accumulate in TMEM, so every output
 // element is written once by one CTA: results are deterministic, with no
-// atomics and no fp32 scratch beyond delta.
+// atomics; the only scratch is the padded row-statistics workspace.
 #include "rt_device.cuh"
 #include "rt_internal.h"
 
@@ -20,8 +20,6 @@ namespace bwd {
 
 constexpr int kThreads = 192;
 constexpr int kTmemCols = 512;
-
-__device__ __forceinline__ void softmax_group_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 template <int DH>
 struct Cfg {
@@ -35,8 +33,12 @@ struct Cfg {
   static constexpr int kA1 = kTileBytes;
   static constexpr int kR0 = 2 * kTileBytes;                 // ring tensor 0 (K or Q)
   static constexpr int kR1 = kR0 + kStages * kTileBytes;    // ring tensor 1 (V or dO)
-  static constexpr int kSmemBytes = kR1 + kStages * kTileBytes;
-  static constexpr int kDynSmem = kSmemBytes + 1024;
+  static constexpr int kRL = kR1 + kStages * kTileBytes;    // ring: lse2[128], delta[128] per stage
+  static constexpr int kRowStatBytes = 2 * RT_TILE * 4;
+  static constexpr int kSmemBytes = kRL + kStages * kRowStatBytes;
+  // 512 TMEM columns per CTA: ask for enough shared memory that a second CTA
+  // never lands on the same SM (it would only block in tcgen05.alloc).
+  static constexpr int kDynSmem = (kSmemBytes + 1024) > 118 * 1024 ? (kSmemBytes + 1024) : 118 * 1024;
 };
 
 struct __align__(8) Barriers {
@@ -49,16 +51,25 @@ struct __align__(8) Barriers {
   uint64_t drain;
 };
 
+// Row statistics for the gradient kernels, padded to whole tiles:
+//   stats[bh][0][q] = lse[bh][q] * log2(e)   (0 for q >= S)
+//   stats[bh][1][q] = sum_d dO[bh][q][d] * O[bh][q][d]   (0 for q >= S)
 template <int DH>
-__global__ void __launch_bounds__(256) delta_kernel(const uint16_t* __restrict__ o,
-                                                    const uint16_t* __restrict__ d_o,
-                                                    float* __restrict__ delta, long long rows) {
+__global__ void __launch_bounds__(256) row_stats_kernel(const uint16_t* __restrict__ o,
+                                                        const uint16_t* __restrict__ d_o,
+                                                        const float* __restrict__ lse,
+                                                        float* __restrict__ stats, int S, int Sp,
+                                                        long long rows_padded) {
   constexpr int kLanesPerRow = DH / 8;
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const long long row = gid / kLanesPerRow;
+  const long long prow = gid / kLanesPerRow;
   const int sub = (int)(gid % kLanesPerRow);
+  const long long bh = prow / Sp;
+  const int q = (int)(prow % Sp);
+  const bool in = prow < rows_padded && q < S;
   float acc = 0.f;
-  if (row < rows) {
+  if (in) {
+    const long long row = bh * S + q;
     const uint4 a = *reinterpret_cast<const uint4*>(o + row * DH + sub * 8);
     const uint4 g = *reinterpret_cast<const uint4*>(d_o + row * DH + sub * 8);
     const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
@@ -73,7 +84,11 @@ __global__ void __launch_bounds__(256) delta_kernel(const uint16_t* __restrict__
   }
 #pragma unroll
   for (int off = kLanesPerRow / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, off);
-  if (row < rows && sub == 0) delta[row] = acc;
+  if (prow < rows_padded && sub == 0) {
+    float* st = stats + bh * 2 * Sp;
+    st[q] = in ? lse[bh * S + q] * 1.4426950408889634f : 0.f;
+    st[Sp + q] = acc;
+  }
 }
 
 __device__ __forceinline__ void store_row_bf16(uint16_t* dst, const uint32_t (&pk)[8]) {
@@ -91,7 +106,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
               const rt_tile_plan plan, int H, int S, float scale, float scale_log2,
-              const float* __restrict__ lse, const float* __restrict__ delta, uint16_t* __restrict__ dq) {
+              const float* __restrict__ stats, uint16_t* __restrict__ dq) {
   using C = Cfg<DH>;
   constexpr int kS = 0, kDP = 128, kDS = 256, kDQ = 320;
   extern __shared__ uint8_t smem_raw[];
@@ -200,8 +215,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = qt * RT_TILE + row;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const uint32_t* masks = plan.tile_masks + ((size_t)row_list * T) * RT_TILE * 4;
-    const float lse2 = q < S ? lse[(size_t)bh * S + q] * 1.4426950408889634f : 0.f;
-    const float dlt = q < S ? delta[(size_t)bh * S + q] : 0.f;
+    const int Sp = T * RT_TILE;
+    const float lse2 = stats[(size_t)bh * 2 * Sp + q];
+    const float dlt = stats[(size_t)bh * 2 * Sp + Sp + q];
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int ent = list[j];
@@ -268,8 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                 const rt_tile_plan plan, int H, int S, float scale, float scale_log2,
-                const float* __restrict__ lse, const float* __restrict__ delta, uint16_t* __restrict__ dk,
-                uint16_t* __restrict__ dv) {
+                const float* __restrict__ stats, uint16_t* __restrict__ dk, uint16_t* __restrict__ dv) {
   using C = Cfg<DH>;
   constexpr int kST = 0, kDPT = 128, kPT = 256, kDST = 320, kDV = 384, kDK = 384 + DH;
   extern __shared__ uint8_t smem_raw[];
@@ -277,8 +292,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ Barriers bars;
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_flag;
-  __shared__ float s_lse2[2][RT_TILE];
-  __shared__ float s_dlt[2][RT_TILE];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int T = plan.tiles;
@@ -287,6 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int list_begin = plan.k2q_ptr[col_list];
   const int n_tiles = plan.k2q_ptr[col_list + 1] - list_begin;
   const int* list = plan.k2q_idx + list_begin;
+  const int Sp = T * RT_TILE;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -320,9 +334,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = i % C::kStages;
         if (i >= C::kStages && !mbar_wait(&bars.ring_empty[s], ((i / C::kStages) - 1) & 1, &abort_flag)) break;
         const int qtile = list[i] & 0x7FFFFFFF;
-        mbar_arrive_expect_tx(&bars.ring_full[s], 2 * C::kTileBytes);
+        mbar_arrive_expect_tx(&bars.ring_full[s], 2 * C::kTileBytes + C::kRowStatBytes);
         tma_load_3d(smem + C::kR0 + s * C::kTileBytes, &tm_q, &bars.ring_full[s], 0, qtile * RT_TILE, bh);
         tma_load_3d(smem + C::kR1 + s * C::kTileBytes, &tm_do, &bars.ring_full[s], 0, qtile * RT_TILE, bh);
+        uint8_t* st = smem + C::kRL + s * C::kRowStatBytes;
+        const float* src = stats + (size_t)bh * 2 * Sp + (size_t)qtile * RT_TILE;
+        bulk_load(st, src, RT_TILE * 4, &bars.ring_full[s]);
+        bulk_load(st + RT_TILE * 4, src + Sp, RT_TILE * 4, &bars.ring_full[s]);
       }
       volatile int no_abort = 0;
       for (int ii = max(0, i - C::kStages); ii < i; ++ii)
@@ -381,7 +399,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     const int quad = warp & 3;
     const int row = quad * 32 + lane;           // key within the tile
-    const int t = threadIdx.x - 64;             // 0..127, loader index for lse / delta
     const int key = kt * RT_TILE + row;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const uint32_t* masks_t = plan.tile_masks_t + ((size_t)col_list * T) * RT_TILE * 4;
@@ -389,17 +406,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < n_tiles; ++i) {
       const int ent = list[i];
       const int qtile = ent & 0x7FFFFFFF;
-      {
-        const int qi = qtile * RT_TILE + t;
-        s_lse2[i & 1][t] = qi < S ? lse[(size_t)bh * S + qi] * 1.4426950408889634f : 0.f;
-        s_dlt[i & 1][t] = qi < S ? delta[(size_t)bh * S + qi] : 0.f;
-      }
       uint4 mk = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
       if (ent >= 0) mk = *reinterpret_cast<const uint4*>(masks_t + ((size_t)qtile * RT_TILE + row) * 4);
       const uint32_t mw[4] = {mk.x, mk.y, mk.z, mk.w};
-      softmax_group_sync();
-      const float* l2 = s_lse2[i & 1];
-      const float* dl = s_dlt[i & 1];
+      const int stage = i % C::kStages;
+      if (!(ok = mbar_wait(&bars.ring_full[stage], (i / C::kStages) & 1, &abort_flag))) break;
+      const float* l2 = reinterpret_cast<const float*>(smem + C::kRL + stage * C::kRowStatBytes);
+      const float* dl = l2 + RT_TILE;
       if (!(ok = mbar_wait(&bars.s_full, i & 1, &abort_flag))) break;
       if (i > 0 && !(ok = mbar_wait(&bars.mma_done, (i - 1) & 1, &abort_flag))) break;
       tc_fence_after();
@@ -461,43 +474,46 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int DH>
 int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* o, const uint16_t* d_o,
            const float* lse, int B, int H, int S, float scale, const rt_tile_plan& plan, uint16_t* dq,
-           uint16_t* dk, uint16_t* dv, float* delta, cudaStream_t stream) {
+           uint16_t* dk, uint16_t* dv, float* stats, cudaStream_t stream) {
   using C = Cfg<DH>;
   CUtensorMap tq, tk, tv, tdo;
   if (make_qkv_tensor_map(&tq, q, B * H, S, DH) != RT_OK || make_qkv_tensor_map(&tk, k, B * H, S, DH) != RT_OK ||
       make_qkv_tensor_map(&tv, v, B * H, S, DH) != RT_OK || make_qkv_tensor_map(&tdo, d_o, B * H, S, DH) != RT_OK)
-    return RT_ERR_CUDA;
+    return RT_ERR_CUDA;  // detail recorded by make_qkv_tensor_map
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(dq_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kDynSmem) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(dkdv_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kDynSmem) !=
-            cudaSuccess)
-      return RT_ERR_CUDA;
+    cudaError_t e = cudaFuncSetAttribute(dq_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kDynSmem);
+    if (e != cudaSuccess) return cuda_failure(e, "cudaFuncSetAttribute(dq_kernel)");
+    e = cudaFuncSetAttribute(dkdv_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kDynSmem);
+    if (e != cudaSuccess) return cuda_failure(e, "cudaFuncSetAttribute(dkdv_kernel)");
     configured[dev] = true;
   }
-  const long long rows = (long long)B * H * S;
-  const long long threads = rows * (DH / 8);
-  delta_kernel<DH><<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(o, d_o, delta, rows);
+  const int Sp = plan.tiles * RT_TILE;
+  const long long rows_padded = (long long)B * H * Sp;
+  const long long threads = rows_padded * (DH / 8);
+  row_stats_kernel<DH><<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(o, d_o, lse, stats, S, Sp,
+                                                                              rows_padded);
+  if (int st = check_launch("row_stats_kernel launch")) return st;
   const float scale_log2 = scale * 1.4426950408889634f;
   dim3 grid(plan.tiles, H, B);
-  dkdv_kernel<DH><<<grid, kThreads, C::kDynSmem, stream>>>(tq, tk, tv, tdo, plan, H, S, scale, scale_log2, lse,
-                                                            delta, dk, dv);
-  dq_kernel<DH><<<grid, kThreads, C::kDynSmem, stream>>>(tq, tk, tv, tdo, plan, H, S, scale, scale_log2, lse,
-                                                          delta, dq);
-  return cudaGetLastError() == cudaSuccess ? RT_OK : RT_ERR_CUDA;
+  dkdv_kernel<DH><<<grid, kThreads, C::kDynSmem, stream>>>(tq, tk, tv, tdo, plan, H, S, scale, scale_log2,
+                                                            stats, dk, dv);
+  if (int st = check_launch("dkdv_kernel launch")) return st;
+  dq_kernel<DH><<<grid, kThreads, C::kDynSmem, stream>>>(tq, tk, tv, tdo, plan, H, S, scale, scale_log2, stats,
+                                                          dq);
+  return check_launch("dq_kernel launch");
 }
 
 }  // namespace bwd
 
 int launch_attention_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* o,
                          const uint16_t* d_o, const float* lse, int B, int H, int S, int Dh, float scale,
-                         const rt_tile_plan& plan, uint16_t* dq, uint16_t* dk, uint16_t* dv, float* delta,
+                         const rt_tile_plan& plan, uint16_t* dq, uint16_t* dk, uint16_t* dv, float* stats,
                          cudaStream_t stream) {
-  if (Dh == 64) return bwd::launch<64>(q, k, v, o, d_o, lse, B, H, S, scale, plan, dq, dk, dv, delta, stream);
-  if (Dh == 32) return bwd::launch<32>(q, k, v, o, d_o, lse, B, H, S, scale, plan, dq, dk, dv, delta, stream);
+  if (Dh == 64) return bwd::launch<64>(q, k, v, o, d_o, lse, B, H, S, scale, plan, dq, dk, dv, stats, stream);
+  if (Dh == 32) return bwd::launch<32>(q, k, v, o, d_o, lse, B, H, S, scale, plan, dq, dk, dv, stats, stream);
   return RT_ERR_UNSUPPORTED;
 }
 

@@ -39,7 +39,9 @@ struct Cfg {
   static constexpr int kKOff = kTileBytes;
   static constexpr int kVOff = kKOff + kStages * kTileBytes;
   static constexpr int kSmemBytes = kVOff + kStages * kTileBytes;
-  static constexpr int kDynSmem = kSmemBytes + 1024;  // alignment slack
+  // 256 TMEM columns per CTA: at most two CTAs may share an SM, so ask for
+  // enough shared memory that a third never lands there.
+  static constexpr int kDynSmem = (kSmemBytes + 1024) > 78 * 1024 ? (kSmemBytes + 1024) : 78 * 1024;
 };
 
 struct __align__(8) Barriers {
@@ -283,20 +285,20 @@ int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H
   CUtensorMap tq, tk, tv;
   if (make_qkv_tensor_map(&tq, q, B * H, S, DH) != RT_OK || make_qkv_tensor_map(&tk, k, B * H, S, DH) != RT_OK ||
       make_qkv_tensor_map(&tv, v, B * H, S, DH) != RT_OK)
-    return RT_ERR_CUDA;
+    return RT_ERR_CUDA;  // detail recorded by make_qkv_tensor_map
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(attn_fwd_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kDynSmem) !=
-        cudaSuccess)
-      return RT_ERR_CUDA;
+    const cudaError_t e =
+        cudaFuncSetAttribute(attn_fwd_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kDynSmem);
+    if (e != cudaSuccess) return cuda_failure(e, "cudaFuncSetAttribute(attn_fwd_kernel)");
     configured[dev] = true;
   }
   const float scale_log2 = scale * 1.4426950408889634f;
   dim3 grid(plan.tiles, H, B);
   attn_fwd_kernel<DH><<<grid, kThreads, C::kDynSmem, stream>>>(tq, tk, tv, plan, H, S, scale_log2, o, lse);
-  return cudaGetLastError() == cudaSuccess ? RT_OK : RT_ERR_CUDA;
+  return check_launch("attn_fwd_kernel launch");
 }
 
 }  // namespace fwd

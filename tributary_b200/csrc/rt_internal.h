@@ -7,6 +7,15 @@
 
 namespace rt {
 
+// Records the failing CUDA call for rt_last_error() (thread-local) and
+// returns RT_ERR_CUDA.
+int cuda_failure(cudaError_t err, const char* site);
+int driver_failure(int err, const char* site);
+inline int check_launch(const char* site) {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? RT_OK : cuda_failure(e, site);
+}
+
 int launch_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids, const int32_t* column_ids,
                            const uint8_t* is_padding, const uint8_t* fk_adj, int B, int S, int R,
                            int kind, const rt_tile_plan& plan, cudaStream_t stream);

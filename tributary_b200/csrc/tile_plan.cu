@@ -239,9 +239,9 @@ int launch_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids, co
   const int T = plan.tiles;
   const int W = plan.words;
   const int WR = (R + 31) / 32;
-  if (cudaMemsetAsync(plan.live_bits, 0, sizeof(uint32_t) * (size_t)B * T * W, stream) != cudaSuccess ||
-      cudaMemsetAsync(plan.full_bits, 0, sizeof(uint32_t) * (size_t)B * T * W, stream) != cudaSuccess)
-    return RT_ERR_CUDA;
+  cudaError_t e = cudaMemsetAsync(plan.live_bits, 0, sizeof(uint32_t) * (size_t)B * T * W, stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(plan.full_bits, 0, sizeof(uint32_t) * (size_t)B * T * W, stream);
+  if (e != cudaSuccess) return cuda_failure(e, "cudaMemsetAsync(tile bitmaps)");
   const uint32_t* fk_bits = nullptr;
   if ((kind == RT_MASK_FEATURE || kind == RT_MASK_NEIGHBOR) && R > 0) {
     fk_pack_kernel<<<dim3(R, B), 32, 0, stream>>>(fk_adj, R, WR, kind == RT_MASK_NEIGHBOR ? 1 : 0,
@@ -251,7 +251,7 @@ int launch_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids, co
   tile_mask_kernel<<<dim3(T, T, B), RT_TILE, 0, stream>>>(perm, seq_row_ids, column_ids, is_padding,
                                                            fk_bits, S, R, WR, kind, plan);
   tile_list_kernel<<<1, 1024, 0, stream>>>(plan);
-  return cudaGetLastError() == cudaSuccess ? RT_OK : RT_ERR_CUDA;
+  return check_launch("tile plan kernels launch");
 }
 
 }  // namespace rt
