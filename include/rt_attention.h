@@ -127,6 +127,23 @@ int rt_attention_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, co
                      uint16_t* dq, uint16_t* dk, uint16_t* dv, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* Backward for callers that cannot allocate device memory (no counterpart in
+ * the reference). Same arguments and results as rt_attention_bwd minus the
+ * workspace: a plugin host or FFI handler without a scratch-allocation hook,
+ * or a service that may not call cudaMalloc after start-up, cannot provide
+ * that workspace, so this variant keeps it in an 8 MB array compiled into the
+ * library (held by every GPU that loads the library until exit). Problems
+ * with batch * heads * (seq_len rounded up to 128) > 2^20 return
+ * RT_ERR_WORKSPACE. All calls on a device share the array: calls that
+ * overlap on the GPU race and must be ordered (one stream or events). The
+ * first call on each device looks up the array's address and should come
+ * before any stream capture. Allocates nothing. */
+int rt_attention_bwd_noalloc(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                             const uint16_t* o, const uint16_t* d_o, const float* lse,
+                             int32_t batch, int32_t heads, int32_t seq_len, int32_t head_dim,
+                             float scale, const rt_tile_plan* plan, uint16_t* dq, uint16_t* dk,
+                             uint16_t* dv, void* stream);
+
 /* Sticky device status (RT_OK or RT_ERR_TIMEOUT) raised by any kernel of the
  * library on the current device. Synchronises the device. If `reset` is
  * non-zero the status is cleared after reading. */

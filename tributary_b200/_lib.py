@@ -30,6 +30,7 @@ TILE = 128
 EXPORTED = (
     "rt_tile_plan_bytes", "rt_tile_plan_bind", "rt_build_tile_plan",
     "rt_attention_fwd", "rt_attention_bwd_workspace_bytes", "rt_attention_bwd",
+    "rt_attention_bwd_noalloc",
     "rt_device_status", "rt_status_string", "rt_last_error", "rt_version",
 )
 
@@ -79,6 +80,9 @@ def _declare(lib):
     lib.rt_attention_bwd.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, plan_p,
                                      vp, vp, vp, vp, sz, vp]
     lib.rt_attention_bwd.restype = ctypes.c_int
+    lib.rt_attention_bwd_noalloc.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32,
+                                             plan_p, vp, vp, vp, vp]
+    lib.rt_attention_bwd_noalloc.restype = ctypes.c_int
     lib.rt_device_status.argtypes = [i32]
     lib.rt_device_status.restype = ctypes.c_int
     lib.rt_status_string.argtypes = [i32]

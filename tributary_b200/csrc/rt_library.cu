@@ -6,3 +6,4 @@
 #include "attn_fwd.cu"
 #include "attn_bwd.cu"
 #include "api.cu"
+#include "attn_bwd_noalloc.cu"
