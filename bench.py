@@ -210,6 +210,8 @@ class Workload:
                 events["bwd"][1].record()
                 for name in ("plan", "fwd", "bwd"):
                     events["acc"][name].append((events[name][0], events[name][1]))
+                    events["by_kind"].setdefault((k["kind"], name), []).append(
+                        (events[name][0], events[name][1]))
                     events[name] = (self.torch.cuda.Event(enable_timing=True),
                                     self.torch.cuda.Event(enable_timing=True))
 
@@ -371,11 +373,14 @@ def run_our_arm(args, cfg):
     ev = {n: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for n in ("plan", "fwd", "bwd")}
     ev["acc"] = {"plan": [], "fwd": [], "bwd": []}
+    ev["by_kind"] = {}
     for _ in range(args.steps):
         wl.step(events=ev)
     barrier(world)
     clocks = sampler.stop()
     part_ms = {n: sum(a.elapsed_time(b) for a, b in ev["acc"][n]) / args.steps for n in ("plan", "fwd", "bwd")}
+    kind_ms = {KIND_NAMES[kk]: {n: sum(a.elapsed_time(b) for a, b in ev["by_kind"][(kk, n)]) / args.steps
+                                for n in ("plan", "fwd", "bwd")} for kk in range(4)}
     step_ms = max_over_ranks(step_ms, world)
     part_ms = {n: max_over_ranks(v, world) for n, v in part_ms.items()}
 
@@ -420,6 +425,7 @@ def run_our_arm(args, cfg):
             "tflops_live_tiles": achieved_tf,
             "frac_of_bf16_peak": achieved_tf / peak_tf,
             "breakdown_ms_per_step": part_ms,
+            "breakdown_ms_by_kind": kind_ms,
             "roofline": {"bound": "tensor", "kernel": "attention fwd+bwd (attn_fwd, row_stats, dkdv, dq)",
                          "achieved": achieved_tf, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": achieved_tf / peak_tf, "peak_source": peak_src + " bf16 dense (burst)",
@@ -448,10 +454,15 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the workload's batch size (profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.batch is not None:
+        cfg["B"] = args.batch
+        cfg["name"] = cfg["name"].replace("_b%d_" % CONFIGS[args.config]["B"], "_b%d_" % args.batch)
     if args.impl == "reference":
         run_reference_arm(args, cfg)
     else:

@@ -9,7 +9,8 @@
 //   dV      = P^T dO ; dK = scale * dS^T Q             (dkdv_kernel: thread = key)
 //
 // Both gradient kernels recompute P from lse, iterate only live tiles (q2k
-// list for dQ, k2q list for dK/dV) and accumulate in TMEM, so every output
+// list for dQ, k2q list for dK/dV), double-buffer S in tensor memory so the
+// next tile's QK^T overlaps the exponentials, and accumulate in TMEM, so every output
 // element is written once by one CTA: results are deterministic, with no
 // atomics; the only scratch is the padded row-statistics workspace.
 #include "rt_device.cuh"
@@ -41,19 +42,112 @@ struct Cfg {
   static constexpr int kDynSmem = (kSmemBytes + 1024) > 118 * 1024 ? (kSmemBytes + 1024) : 118 * 1024;
 };
 
+constexpr int kMaxTiles = 65536 / RT_TILE;
+
 struct __align__(8) Barriers {
-  uint64_t res_full;
-  uint64_t ring_full[4];
-  uint64_t ring_empty[4];
-  uint64_t s_full;
-  uint64_t p_full;
-  uint64_t mma_done;
+  uint64_t res_full;       // resident pair loaded (Q,dO for dQ; K,V for dK/dV)
+  uint64_t ring_full[4];   // ring stage loaded
+  uint64_t ring_empty[4];  // ring stage released by the MMAs
+  uint64_t st_full[2];     // S (or S^T) buffer b computed
+  uint64_t dp_full;        // dP (or dP^T) computed
+  uint64_t pa_full;        // softmax phase A done: S buffer read (and P^T written)
+  uint64_t pb_full;        // softmax phase B done: dS (or dS^T) written
+  uint64_t done;           // last gradient MMA complete
   uint64_t drain;
 };
 
-// Row statistics for the gradient kernels, padded to whole tiles:
-//   stats[bh][0][q] = lse[bh][q] * log2(e)   (0 for q >= S)
-//   stats[bh][1][q] = sum_d dO[bh][q][d] * O[bh][q][d]   (0 for q >= S)
+__device__ __forceinline__ void init_barriers(Barriers& bars, int stages) {
+  mbar_init(&bars.res_full, 1);
+  for (int s = 0; s < stages; ++s) {
+    mbar_init(&bars.ring_full[s], 1);
+    mbar_init(&bars.ring_empty[s], 1);
+  }
+  mbar_init(&bars.st_full[0], 1);
+  mbar_init(&bars.st_full[1], 1);
+  mbar_init(&bars.dp_full, 1);
+  mbar_init(&bars.pa_full, 128);
+  mbar_init(&bars.pb_full, 128);
+  mbar_init(&bars.done, 1);
+  mbar_init(&bars.drain, 1);
+  fence_mbar_init();
+}
+
+// Softmax phase A for one 128x128 tile held in TMEM (one row per thread):
+// p = exp2(c * s + nl) with nl = -lse * log2(e), masked entries 0, packed as
+// bf16 pairs. `nl_col` (per column, from shared memory) is used when the
+// rows of the tile are keys (dK/dV), `nl_row` when they are queries (dQ).
+template <bool kPerColumn>
+__device__ __forceinline__ void softmax_phase_a(uint32_t taddr, bool full, const uint4& mk, float c,
+                                                const float* nl_col, float nl_row, uint32_t (&pk)[64]) {
+  uint32_t r[128];
+  {
+    uint32_t (&r0)[64] = *reinterpret_cast<uint32_t(*)[64]>(&r[0]);
+    uint32_t (&r1)[64] = *reinterpret_cast<uint32_t(*)[64]>(&r[64]);
+    tmem_ld64(taddr, r0);
+    tmem_ld64(taddr + 64, r1);
+  }
+  tmem_wait_ld();
+  if (!full) {
+    const uint32_t mw[4] = {mk.x, mk.y, mk.z, mk.w};
+#pragma unroll
+    for (int e = 0; e < 128; ++e) r[e] = ((mw[e >> 5] >> (e & 31)) & 1u) ? r[e] : __float_as_uint(-INFINITY);
+  }
+  const float2 c2 = make_float2(c, c);
+#pragma unroll
+  for (int e = 0; e < 128; e += 4) {
+    float2 nl01, nl23;
+    if (kPerColumn) {
+      const float4 v = *reinterpret_cast<const float4*>(nl_col + e);
+      nl01 = make_float2(v.x, v.y);
+      nl23 = make_float2(v.z, v.w);
+    } else {
+      nl01 = nl23 = make_float2(nl_row, nl_row);
+    }
+    const float2 x01 = ffma2(make_float2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), c2, nl01);
+    const float2 x23 = ffma2(make_float2(__uint_as_float(r[e + 2]), __uint_as_float(r[e + 3])), c2, nl23);
+    pk[e >> 1] = pack_bf16x2(fast_exp2(x01.x), fast_exp2(x01.y));
+    pk[(e >> 1) + 1] = pack_bf16x2(fast_exp2(x23.x), fast_exp2(x23.y));
+  }
+}
+
+// Softmax phase B: dS = P * (dP - delta) from the dP tile in TMEM, written
+// back as bf16 pairs into the first 64 columns of the same TMEM block (each
+// 32-column chunk is read before the 16 columns it lands on are written).
+template <bool kPerColumn>
+__device__ __forceinline__ void softmax_phase_b(uint32_t taddr, const uint32_t (&pk)[64], const float* nd_col,
+                                                float nd_row) {
+#pragma unroll
+  for (int ch = 0; ch < 4; ++ch) {
+    uint32_t d[32];
+    tmem_ld32(taddr + ch * 32, d);
+    tmem_wait_ld();
+    uint32_t ds[16];
+#pragma unroll
+    for (int e = 0; e < 32; e += 4) {
+      float2 nd01, nd23;
+      if (kPerColumn) {
+        const float4 v = *reinterpret_cast<const float4*>(nd_col + ch * 32 + e);
+        nd01 = make_float2(v.x, v.y);
+        nd23 = make_float2(v.z, v.w);
+      } else {
+        nd01 = nd23 = make_float2(nd_row, nd_row);
+      }
+      const float2 g01 = fmul2(unpack_bf16x2(pk[ch * 16 + (e >> 1)]),
+                               fadd2(make_float2(__uint_as_float(d[e]), __uint_as_float(d[e + 1])), nd01));
+      const float2 g23 = fmul2(unpack_bf16x2(pk[ch * 16 + (e >> 1) + 1]),
+                               fadd2(make_float2(__uint_as_float(d[e + 2]), __uint_as_float(d[e + 3])), nd23));
+      ds[e >> 1] = pack_bf16x2(g01.x, g01.y);
+      ds[(e >> 1) + 1] = pack_bf16x2(g23.x, g23.y);
+    }
+    tmem_st16(taddr + ch * 16, ds);
+  }
+}
+
+
+// Row statistics for the gradient kernels, padded to whole tiles and stored
+// negated so they enter the exponent / difference as FMA addends:
+//   stats[bh][0][q] = -lse[bh][q] * log2(e)                 (0 for q >= S)
+//   stats[bh][1][q] = -sum_d dO[bh][q][d] * O[bh][q][d]     (0 for q >= S)
 template <int DH>
 __global__ void __launch_bounds__(256) row_stats_kernel(const uint16_t* __restrict__ o,
                                                         const uint16_t* __restrict__ d_o,
@@ -86,8 +180,8 @@ __global__ void __launch_bounds__(256) row_stats_kernel(const uint16_t* __restri
   for (int off = kLanesPerRow / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, off);
   if (prow < rows_padded && sub == 0) {
     float* st = stats + bh * 2 * Sp;
-    st[q] = in ? lse[bh * S + q] * 1.4426950408889634f : 0.f;
-    st[Sp + q] = acc;
+    st[q] = in ? -lse[bh * S + q] * 1.4426950408889634f : 0.f;
+    st[Sp + q] = -acc;
   }
 }
 
@@ -99,7 +193,11 @@ __device__ __forceinline__ void store_row_bf16(uint16_t* dst, const uint32_t (&p
 
 // ---------------------------------------------------------------------------
 // dQ: one CTA per (b, h, q-tile); thread = query row.
-// TMEM: S [0,128) fp32, dP [128,256) fp32, dS [256,320) bf16x2, dQ [320,320+DH).
+// TMEM: S0 [0,128), S1 [128,256) fp32 (double buffered), dP [256,384) fp32
+// with dS written over its first 64 columns as bf16 pairs, dQ [384,384+DH).
+// Per k-tile j: the MMA thread issues S_{j+1} as soon as softmax phase A has
+// read S_j, so QK^T overlaps phase B; dP_{j+1} follows dQ += dS_j K_j and
+// overlaps the next phase A.
 // ---------------------------------------------------------------------------
 template <int DH>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -108,12 +206,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               const rt_tile_plan plan, int H, int S, float scale, float scale_log2,
               const float* __restrict__ stats, uint16_t* __restrict__ dq) {
   using C = Cfg<DH>;
-  constexpr int kS = 0, kDP = 128, kDS = 256, kDQ = 320;
+  constexpr int kS0 = 0, kDP = 256, kDQ = 384;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ Barriers bars;
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_flag;
+  __shared__ int s_list[kMaxTiles];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int T = plan.tiles;
@@ -121,20 +220,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int row_list = b * T + qt;
   const int list_begin = plan.q2k_ptr[row_list];
   const int n_tiles = plan.q2k_ptr[row_list + 1] - list_begin;
-  const int* list = plan.q2k_idx + list_begin;
+  for (int i = threadIdx.x; i < n_tiles; i += kThreads) s_list[i] = plan.q2k_idx[list_begin + i];
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
-    mbar_init(&bars.res_full, 1);
-    for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(&bars.ring_full[s], 1);
-      mbar_init(&bars.ring_empty[s], 1);
-    }
-    mbar_init(&bars.s_full, 1);
-    mbar_init(&bars.p_full, 128);
-    mbar_init(&bars.mma_done, 1);
-    mbar_init(&bars.drain, 1);
-    fence_mbar_init();
+    init_barriers(bars, C::kStages);
   }
   if (warp == 0) {
     tmem_alloc(&tmem_base_s, kTmemCols);
@@ -154,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (; j < n_tiles; ++j) {
         const int s = j % C::kStages;
         if (j >= C::kStages && !mbar_wait(&bars.ring_empty[s], ((j / C::kStages) - 1) & 1, &abort_flag)) break;
-        const int kt = list[j] & 0x7FFFFFFF;
+        const int kt = s_list[j] & 0x7FFFFFFF;
         mbar_arrive_expect_tx(&bars.ring_full[s], 2 * C::kTileBytes);
         tma_load_3d(smem + C::kR0 + s * C::kTileBytes, &tm_k, &bars.ring_full[s], 0, kt * RT_TILE, bh);
         tma_load_3d(smem + C::kR1 + s * C::kTileBytes, &tm_v, &bars.ring_full[s], 0, kt * RT_TILE, bh);
@@ -170,41 +260,50 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc_q = idesc_bf16_f32(128, DH, false, true);
       const uint32_t q_addr = smem_u32(smem + C::kA0);
       const uint32_t do_addr = smem_u32(smem + C::kA1);
-      bool ok = mbar_wait(&bars.res_full, 0, &abort_flag);
+      auto k_addr = [&](int j) { return smem_u32(smem + C::kR0 + (j % C::kStages) * C::kTileBytes); };
+      auto v_addr = [&](int j) { return smem_u32(smem + C::kR1 + (j % C::kStages) * C::kTileBytes); };
+      auto issue_s = [&](int j) {  // S[j%2] = Q K_j^T
+#pragma unroll
+        for (int ks = 0; ks < DH / 16; ++ks)
+          mma_ss(tmem + kS0 + (j & 1) * 128, sdesc(q_addr + ks * 32, 16, C::kSBO, C::kSwizzle),
+                 sdesc(k_addr(j) + ks * 32, 16, C::kSBO, C::kSwizzle), idesc_s, ks > 0 ? 1u : 0u);
+        mma_commit(&bars.st_full[j & 1]);
+      };
+      auto issue_dp = [&](int j) {  // dP = dO V_j^T
+#pragma unroll
+        for (int ks = 0; ks < DH / 16; ++ks)
+          mma_ss(tmem + kDP, sdesc(do_addr + ks * 32, 16, C::kSBO, C::kSwizzle),
+                 sdesc(v_addr(j) + ks * 32, 16, C::kSBO, C::kSwizzle), idesc_s, ks > 0 ? 1u : 0u);
+        mma_commit(&bars.dp_full);
+      };
+      bool ok = mbar_wait(&bars.res_full, 0, &abort_flag) && mbar_wait(&bars.ring_full[0], 0, &abort_flag);
       tc_fence_after();
-      for (int j = 0; ok && j <= n_tiles; ++j) {
-        if (j > 0) {
-          if (!(ok = mbar_wait(&bars.p_full, (j - 1) & 1, &abort_flag))) break;
-          tc_fence_after();
-          const int sp = (j - 1) % C::kStages;
-          const uint32_t k_addr = smem_u32(smem + C::kR0 + sp * C::kTileBytes);
-#pragma unroll
-          for (int ks = 0; ks < RT_TILE / 16; ++ks) {
-            const uint64_t bdesc = sdesc(k_addr + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle);
-            mma_ts(tmem + kDQ, tmem + kDS + ks * 8, bdesc, idesc_q, (j > 1 || ks > 0) ? 1u : 0u);
-          }
-          mma_commit(&bars.mma_done);
-          mma_commit(&bars.ring_empty[sp]);
-        }
-        if (j < n_tiles) {
-          const int s = j % C::kStages;
-          if (!(ok = mbar_wait(&bars.ring_full[s], (j / C::kStages) & 1, &abort_flag))) break;
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(smem + C::kR0 + s * C::kTileBytes);
-          const uint32_t v_addr = smem_u32(smem + C::kR1 + s * C::kTileBytes);
-#pragma unroll
-          for (int ks = 0; ks < DH / 16; ++ks) {
-            mma_ss(tmem + kS, sdesc(q_addr + ks * 32, 16, C::kSBO, C::kSwizzle),
-                   sdesc(k_addr + ks * 32, 16, C::kSBO, C::kSwizzle), idesc_s, ks > 0 ? 1u : 0u);
-          }
-#pragma unroll
-          for (int ks = 0; ks < DH / 16; ++ks) {
-            mma_ss(tmem + kDP, sdesc(do_addr + ks * 32, 16, C::kSBO, C::kSwizzle),
-                   sdesc(v_addr + ks * 32, 16, C::kSBO, C::kSwizzle), idesc_s, ks > 0 ? 1u : 0u);
-          }
-          mma_commit(&bars.s_full);
-        }
+      if (ok) {
+        issue_s(0);
+        issue_dp(0);
       }
+      // S_{j+1} is issued only once phase A of tile j has been observed, so no
+      // barrier can run two phases ahead of its waiter.
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        if (!(ok = mbar_wait(&bars.pa_full, j & 1, &abort_flag))) break;
+        tc_fence_after();
+        if (j + 1 < n_tiles) {
+          if (!(ok = mbar_wait(&bars.ring_full[(j + 1) % C::kStages], ((j + 1) / C::kStages) & 1, &abort_flag)))
+            break;
+          tc_fence_after();
+          issue_s(j + 1);
+        }
+        if (!(ok = mbar_wait(&bars.pb_full, j & 1, &abort_flag))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < RT_TILE / 16; ++ks)
+          mma_ts(tmem + kDQ, tmem + kDP + ks * 8,
+                 sdesc(k_addr(j) + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_q,
+                 (j > 0 || ks > 0) ? 1u : 0u);
+        mma_commit(&bars.ring_empty[j % C::kStages]);
+        if (j + 1 < n_tiles) issue_dp(j + 1);
+      }
+      mma_commit(&bars.done);
       mma_commit(&bars.drain);
       volatile int no_abort = 0;
       mbar_wait(&bars.drain, 0, &no_abort);
@@ -216,41 +315,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const uint32_t* masks = plan.tile_masks + ((size_t)row_list * T) * RT_TILE * 4;
     const int Sp = T * RT_TILE;
-    const float lse2 = stats[(size_t)bh * 2 * Sp + q];
-    const float dlt = stats[(size_t)bh * 2 * Sp + Sp + q];
+    const float nl = stats[(size_t)bh * 2 * Sp + q];
+    const float nd = stats[(size_t)bh * 2 * Sp + Sp + q];
+    auto load_mask = [&](int ent) {
+      uint4 mk = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
+      if (ent >= 0) mk = __ldg(reinterpret_cast<const uint4*>(masks + ((size_t)(ent & 0x7FFFFFFF) * RT_TILE + row) * 4));
+      return mk;
+    };
+    uint4 mk_next = n_tiles > 0 ? load_mask(s_list[0]) : make_uint4(0u, 0u, 0u, 0u);
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
-      const int ent = list[j];
-      const int kt = ent & 0x7FFFFFFF;
-      uint4 mk = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
-      if (ent >= 0) mk = *reinterpret_cast<const uint4*>(masks + ((size_t)kt * RT_TILE + row) * 4);
-      const uint32_t mw[4] = {mk.x, mk.y, mk.z, mk.w};
-      if (!(ok = mbar_wait(&bars.s_full, j & 1, &abort_flag))) break;
-      if (j > 0 && !(ok = mbar_wait(&bars.mma_done, (j - 1) & 1, &abort_flag))) break;
+      const bool full = s_list[j] < 0;
+      const uint4 mk = mk_next;
+      if (j + 1 < n_tiles) mk_next = load_mask(s_list[j + 1]);
+      if (!(ok = mbar_wait(&bars.st_full[j & 1], (j >> 1) & 1, &abort_flag))) break;
       tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t rs[32], rp[32];
-        tmem_ld32(lane_base + kS + c * 32, rs);
-        tmem_ld32(lane_base + kDP + c * 32, rp);
-        tmem_wait_ld();
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float p0 = ((mw[c] >> e) & 1u) ? fast_exp2(__uint_as_float(rs[e]) * scale_log2 - lse2) : 0.f;
-          const float p1 =
-              ((mw[c] >> (e + 1)) & 1u) ? fast_exp2(__uint_as_float(rs[e + 1]) * scale_log2 - lse2) : 0.f;
-          const float d0 = p0 * (__uint_as_float(rp[e]) - dlt);
-          const float d1 = p1 * (__uint_as_float(rp[e + 1]) - dlt);
-          pk[e / 2] = pack_bf16x2(d0, d1);
-        }
-        tmem_st16(lane_base + kDS + c * 16, pk);
-      }
+      uint32_t pk[64];
+      softmax_phase_a<false>(lane_base + kS0 + (j & 1) * 128, full, mk, scale_log2, nullptr, nl, pk);
+      tc_fence_before();
+      mbar_arrive(&bars.pa_full);
+      if (!(ok = mbar_wait(&bars.dp_full, j & 1, &abort_flag))) break;
+      tc_fence_after();
+      softmax_phase_b<false>(lane_base + kDP, pk, nullptr, nd);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bars.p_full);
+      mbar_arrive(&bars.pb_full);
     }
-    if (ok && n_tiles > 0 && mbar_wait(&bars.mma_done, (n_tiles - 1) & 1, &abort_flag)) {
+    if (ok && n_tiles > 0 && mbar_wait(&bars.done, 0, &abort_flag)) {
       tc_fence_after();
       uint16_t* dst = dq + ((size_t)bh * S + q) * DH;
 #pragma unroll
@@ -276,8 +367,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---------------------------------------------------------------------------
 // dK, dV: one CTA per (b, h, k-tile); thread = key row.
-// TMEM: S^T [0,128), dP^T [128,256), P^T [256,320) bf16x2, dS^T [320,384) bf16x2,
-//       dV [384,384+DH), dK [384+DH,384+2DH).
+// TMEM: S^T0 [0,128), S^T1 [128,256) fp32 (double buffered; P^T overwrites the
+// first 64 columns as bf16 pairs), dP^T [256,384) fp32 (dS^T overwrites its
+// first 64 columns), dV [384,384+DH), dK [384+DH,384+2DH).
+// Per q-tile i: dV_i and S^T_{i+1} follow softmax phase A (overlapping phase
+// B), dK_i and dP^T_{i+1} follow phase B (overlapping the next phase A).
 // ---------------------------------------------------------------------------
 template <int DH>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -286,12 +380,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const rt_tile_plan plan, int H, int S, float scale, float scale_log2,
                 const float* __restrict__ stats, uint16_t* __restrict__ dk, uint16_t* __restrict__ dv) {
   using C = Cfg<DH>;
-  constexpr int kST = 0, kDPT = 128, kPT = 256, kDST = 320, kDV = 384, kDK = 384 + DH;
+  constexpr int kST0 = 0, kDPT = 256, kDV = 384, kDK = 384 + DH;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ Barriers bars;
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_flag;
+  __shared__ int s_list[kMaxTiles];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int T = plan.tiles;
@@ -299,21 +394,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int col_list = b * T + kt;
   const int list_begin = plan.k2q_ptr[col_list];
   const int n_tiles = plan.k2q_ptr[col_list + 1] - list_begin;
-  const int* list = plan.k2q_idx + list_begin;
   const int Sp = T * RT_TILE;
+  for (int i = threadIdx.x; i < n_tiles; i += kThreads) s_list[i] = plan.k2q_idx[list_begin + i];
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
-    mbar_init(&bars.res_full, 1);
-    for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(&bars.ring_full[s], 1);
-      mbar_init(&bars.ring_empty[s], 1);
-    }
-    mbar_init(&bars.s_full, 1);
-    mbar_init(&bars.p_full, 128);
-    mbar_init(&bars.mma_done, 1);
-    mbar_init(&bars.drain, 1);
-    fence_mbar_init();
+    init_barriers(bars, C::kStages);
   }
   if (warp == 0) {
     tmem_alloc(&tmem_base_s, kTmemCols);
@@ -333,7 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (; i < n_tiles; ++i) {
         const int s = i % C::kStages;
         if (i >= C::kStages && !mbar_wait(&bars.ring_empty[s], ((i / C::kStages) - 1) & 1, &abort_flag)) break;
-        const int qtile = list[i] & 0x7FFFFFFF;
+        const int qtile = s_list[i] & 0x7FFFFFFF;
         mbar_arrive_expect_tx(&bars.ring_full[s], 2 * C::kTileBytes + C::kRowStatBytes);
         tma_load_3d(smem + C::kR0 + s * C::kTileBytes, &tm_q, &bars.ring_full[s], 0, qtile * RT_TILE, bh);
         tma_load_3d(smem + C::kR1 + s * C::kTileBytes, &tm_do, &bars.ring_full[s], 0, qtile * RT_TILE, bh);
@@ -353,96 +439,103 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc_g = idesc_bf16_f32(128, DH, false, true);
       const uint32_t k_addr = smem_u32(smem + C::kA0);
       const uint32_t v_addr = smem_u32(smem + C::kA1);
-      bool ok = mbar_wait(&bars.res_full, 0, &abort_flag);
+      auto q_addr = [&](int i) { return smem_u32(smem + C::kR0 + (i % C::kStages) * C::kTileBytes); };
+      auto do_addr = [&](int i) { return smem_u32(smem + C::kR1 + (i % C::kStages) * C::kTileBytes); };
+      auto issue_st = [&](int i) {  // S^T[i%2] = K Q_i^T
+#pragma unroll
+        for (int ks = 0; ks < DH / 16; ++ks)
+          mma_ss(tmem + kST0 + (i & 1) * 128, sdesc(k_addr + ks * 32, 16, C::kSBO, C::kSwizzle),
+                 sdesc(q_addr(i) + ks * 32, 16, C::kSBO, C::kSwizzle), idesc_s, ks > 0 ? 1u : 0u);
+        mma_commit(&bars.st_full[i & 1]);
+      };
+      auto issue_dpt = [&](int i) {  // dP^T = V dO_i^T
+#pragma unroll
+        for (int ks = 0; ks < DH / 16; ++ks)
+          mma_ss(tmem + kDPT, sdesc(v_addr + ks * 32, 16, C::kSBO, C::kSwizzle),
+                 sdesc(do_addr(i) + ks * 32, 16, C::kSBO, C::kSwizzle), idesc_s, ks > 0 ? 1u : 0u);
+        mma_commit(&bars.dp_full);
+      };
+      bool ok = mbar_wait(&bars.res_full, 0, &abort_flag) && mbar_wait(&bars.ring_full[0], 0, &abort_flag);
       tc_fence_after();
-      for (int i = 0; ok && i <= n_tiles; ++i) {
-        if (i > 0) {
-          if (!(ok = mbar_wait(&bars.p_full, (i - 1) & 1, &abort_flag))) break;
-          tc_fence_after();
-          const int sp = (i - 1) % C::kStages;
-          const uint32_t q_addr = smem_u32(smem + C::kR0 + sp * C::kTileBytes);
-          const uint32_t do_addr = smem_u32(smem + C::kR1 + sp * C::kTileBytes);
-#pragma unroll
-          for (int ks = 0; ks < RT_TILE / 16; ++ks) {
-            const uint32_t acc = (i > 1 || ks > 0) ? 1u : 0u;
-            mma_ts(tmem + kDV, tmem + kPT + ks * 8,
-                   sdesc(do_addr + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_g, acc);
-            mma_ts(tmem + kDK, tmem + kDST + ks * 8,
-                   sdesc(q_addr + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_g, acc);
-          }
-          mma_commit(&bars.mma_done);
-          mma_commit(&bars.ring_empty[sp]);
-        }
-        if (i < n_tiles) {
-          const int s = i % C::kStages;
-          if (!(ok = mbar_wait(&bars.ring_full[s], (i / C::kStages) & 1, &abort_flag))) break;
-          tc_fence_after();
-          const uint32_t q_addr = smem_u32(smem + C::kR0 + s * C::kTileBytes);
-          const uint32_t do_addr = smem_u32(smem + C::kR1 + s * C::kTileBytes);
-#pragma unroll
-          for (int ks = 0; ks < DH / 16; ++ks) {
-            mma_ss(tmem + kST, sdesc(k_addr + ks * 32, 16, C::kSBO, C::kSwizzle),
-                   sdesc(q_addr + ks * 32, 16, C::kSBO, C::kSwizzle), idesc_s, ks > 0 ? 1u : 0u);
-          }
-#pragma unroll
-          for (int ks = 0; ks < DH / 16; ++ks) {
-            mma_ss(tmem + kDPT, sdesc(v_addr + ks * 32, 16, C::kSBO, C::kSwizzle),
-                   sdesc(do_addr + ks * 32, 16, C::kSBO, C::kSwizzle), idesc_s, ks > 0 ? 1u : 0u);
-          }
-          mma_commit(&bars.s_full);
-        }
+      if (ok) {
+        issue_st(0);
+        issue_dpt(0);
       }
+      // S^T_{i+1} is issued only once phase A of tile i has been observed, so
+      // no barrier can run two phases ahead of its waiter.
+      for (int i = 0; ok && i < n_tiles; ++i) {
+        if (!(ok = mbar_wait(&bars.pa_full, i & 1, &abort_flag))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < RT_TILE / 16; ++ks)  // dV += P^T_i dO_i
+          mma_ts(tmem + kDV, tmem + kST0 + (i & 1) * 128 + ks * 8,
+                 sdesc(do_addr(i) + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_g,
+                 (i > 0 || ks > 0) ? 1u : 0u);
+        if (i + 1 < n_tiles) {
+          if (!(ok = mbar_wait(&bars.ring_full[(i + 1) % C::kStages], ((i + 1) / C::kStages) & 1, &abort_flag)))
+            break;
+          tc_fence_after();
+          issue_st(i + 1);
+        }
+        if (!(ok = mbar_wait(&bars.pb_full, i & 1, &abort_flag))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < RT_TILE / 16; ++ks)  // dK += dS^T_i Q_i
+          mma_ts(tmem + kDK, tmem + kDPT + ks * 8,
+                 sdesc(q_addr(i) + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_g,
+                 (i > 0 || ks > 0) ? 1u : 0u);
+        mma_commit(&bars.ring_empty[i % C::kStages]);
+        if (i + 1 < n_tiles) issue_dpt(i + 1);
+      }
+      mma_commit(&bars.done);
       mma_commit(&bars.drain);
       volatile int no_abort = 0;
       mbar_wait(&bars.drain, 0, &no_abort);
     }
   } else {
     const int quad = warp & 3;
-    const int row = quad * 32 + lane;           // key within the tile
+    const int row = quad * 32 + lane;  // key within the tile
     const int key = kt * RT_TILE + row;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const uint32_t* masks_t = plan.tile_masks_t + ((size_t)col_list * T) * RT_TILE * 4;
+    auto load_mask = [&](int ent) {
+      uint4 mk = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
+      if (ent >= 0)
+        mk = __ldg(reinterpret_cast<const uint4*>(masks_t + ((size_t)(ent & 0x7FFFFFFF) * RT_TILE + row) * 4));
+      return mk;
+    };
+    uint4 mk_next = n_tiles > 0 ? load_mask(s_list[0]) : make_uint4(0u, 0u, 0u, 0u);
     bool ok = true;
     for (int i = 0; i < n_tiles; ++i) {
-      const int ent = list[i];
-      const int qtile = ent & 0x7FFFFFFF;
-      uint4 mk = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
-      if (ent >= 0) mk = *reinterpret_cast<const uint4*>(masks_t + ((size_t)qtile * RT_TILE + row) * 4);
-      const uint32_t mw[4] = {mk.x, mk.y, mk.z, mk.w};
+      const bool full = s_list[i] < 0;
+      const uint4 mk = mk_next;
+      if (i + 1 < n_tiles) mk_next = load_mask(s_list[i + 1]);
       const int stage = i % C::kStages;
       if (!(ok = mbar_wait(&bars.ring_full[stage], (i / C::kStages) & 1, &abort_flag))) break;
-      const float* l2 = reinterpret_cast<const float*>(smem + C::kRL + stage * C::kRowStatBytes);
-      const float* dl = l2 + RT_TILE;
-      if (!(ok = mbar_wait(&bars.s_full, i & 1, &abort_flag))) break;
-      if (i > 0 && !(ok = mbar_wait(&bars.mma_done, (i - 1) & 1, &abort_flag))) break;
+      const float* nl = reinterpret_cast<const float*>(smem + C::kRL + stage * C::kRowStatBytes);
+      const float* nd = nl + RT_TILE;
+      if (!(ok = mbar_wait(&bars.st_full[i & 1], (i >> 1) & 1, &abort_flag))) break;
       tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t rs[32], rp[32];
-        tmem_ld32(lane_base + kST + c * 32, rs);
-        tmem_ld32(lane_base + kDPT + c * 32, rp);
-        tmem_wait_ld();
-        uint32_t pk[16], dk_[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const int qa = c * 32 + e;
-          const float p0 =
-              ((mw[c] >> e) & 1u) ? fast_exp2(__uint_as_float(rs[e]) * scale_log2 - l2[qa]) : 0.f;
-          const float p1 =
-              ((mw[c] >> (e + 1)) & 1u) ? fast_exp2(__uint_as_float(rs[e + 1]) * scale_log2 - l2[qa + 1]) : 0.f;
-          const float d0 = p0 * (__uint_as_float(rp[e]) - dl[qa]);
-          const float d1 = p1 * (__uint_as_float(rp[e + 1]) - dl[qa + 1]);
-          pk[e / 2] = pack_bf16x2(p0, p1);
-          dk_[e / 2] = pack_bf16x2(d0, d1);
-        }
-        tmem_st16(lane_base + kPT + c * 16, pk);
-        tmem_st16(lane_base + kDST + c * 16, dk_);
+      uint32_t pk[64];
+      const uint32_t st_addr = lane_base + kST0 + (i & 1) * 128;
+      softmax_phase_a<true>(st_addr, full, mk, scale_log2, nl, 0.f, pk);
+      {
+        uint32_t (&p0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&pk[0]);
+        uint32_t (&p1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&pk[32]);
+        tmem_st32(st_addr, p0);  // P^T over the first 64 columns of its S^T buffer
+        tmem_st32(st_addr + 32, p1);
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bars.p_full);
+      mbar_arrive(&bars.pa_full);
+      if (!(ok = mbar_wait(&bars.dp_full, i & 1, &abort_flag))) break;
+      tc_fence_after();
+      softmax_phase_b<true>(lane_base + kDPT, pk, nd, 0.f);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bars.pb_full);
     }
-    if (ok && n_tiles > 0 && mbar_wait(&bars.mma_done, (n_tiles - 1) & 1, &abort_flag)) {
+    if (ok && n_tiles > 0 && mbar_wait(&bars.done, 0, &abort_flag)) {
       tc_fence_after();
       uint16_t* dst_v = dv + ((size_t)bh * S + key) * DH;
       uint16_t* dst_k = dk + ((size_t)bh * S + key) * DH;

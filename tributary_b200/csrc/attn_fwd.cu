@@ -27,6 +27,7 @@ constexpr int kPCol = 128;
 constexpr int kOCol = 192;
 constexpr int kTmemCols = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by 2^8
+constexpr int kMaxTiles = 65536 / RT_TILE;  // tiles per row of the plan (seq_len <= 65536)
 
 template <int DH>
 struct Cfg {
@@ -65,6 +66,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   __shared__ Barriers bars;
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_flag;
+  __shared__ int s_list[kMaxTiles];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -77,6 +79,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int list_begin = plan.q2k_ptr[row_list];
   const int n_tiles = plan.q2k_ptr[row_list + 1] - list_begin;
   const int* list = plan.q2k_idx + list_begin;
+  for (int i = threadIdx.x; i < n_tiles; i += kThreads) s_list[i] = list[i];
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -112,7 +115,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (; j < n_tiles; ++j) {
         const int s = j % C::kStages;
         if (j >= C::kStages && !mbar_wait(&bars.kv_empty[s], ((j / C::kStages) - 1) & 1, &abort_flag)) break;
-        const int kt = list[j] & 0x7FFFFFFF;
+        const int kt = s_list[j] & 0x7FFFFFFF;
         mbar_arrive_expect_tx(&bars.kv_full[s], 2 * C::kTileBytes);
         tma_load_3d(smem + C::kKOff + s * C::kTileBytes, &tm_k, &bars.kv_full[s], 0, kt * RT_TILE, bh);
         tma_load_3d(smem + C::kVOff + s * C::kTileBytes, &tm_v, &bars.kv_full[s], 0, kt * RT_TILE, bh);
@@ -175,75 +178,85 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int row = quad * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const uint32_t* masks = plan.tile_masks + ((size_t)row_list * T) * RT_TILE * 4;
-    float m_run = -INFINITY;  // running max, log2 units
-    float l_run = 0.f;
+    const float c = scale_log2;
+    const float kNegInf = -INFINITY;
+    float m_run = kNegInf;  // running row max of raw scores (scale not applied)
+    float2 l2 = make_float2(0.f, 0.f);
+    auto load_mask = [&](int ent) {
+      uint4 mk = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
+      if (ent >= 0) mk = __ldg(reinterpret_cast<const uint4*>(masks + ((size_t)(ent & 0x7FFFFFFF) * RT_TILE + row) * 4));
+      return mk;
+    };
+    uint4 mk_next = n_tiles > 0 ? load_mask(s_list[0]) : make_uint4(0u, 0u, 0u, 0u);
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
-      const int ent = list[j];
-      const int kt = ent & 0x7FFFFFFF;
-      uint4 mk = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
-      if (ent >= 0) mk = *reinterpret_cast<const uint4*>(masks + ((size_t)kt * RT_TILE + row) * 4);
-      const uint32_t mw[4] = {mk.x, mk.y, mk.z, mk.w};
+      const bool full = s_list[j] < 0;
+      const uint4 mk = mk_next;
+      if (j + 1 < n_tiles) mk_next = load_mask(s_list[j + 1]);
       if (!(ok = mbar_wait(&bars.s_full, j & 1, &abort_flag))) break;
       tc_fence_after();
-      // pass 1: masked row max of this tile
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(lane_base + kSCol + c * 32, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float v = __uint_as_float(r[e]) * scale_log2;
-          mx = ((mw[c] >> e) & 1u) ? fmaxf(mx, v) : mx;
-        }
+      uint32_t r[128];
+      {
+        uint32_t (&r0)[64] = *reinterpret_cast<uint32_t(*)[64]>(&r[0]);
+        uint32_t (&r1)[64] = *reinterpret_cast<uint32_t(*)[64]>(&r[64]);
+        tmem_ld64(lane_base + kSCol, r0);
+        tmem_ld64(lane_base + kSCol + 64, r1);
       }
+      tmem_wait_ld();
+      if (!full) {
+        const uint32_t mw[4] = {mk.x, mk.y, mk.z, mk.w};
+#pragma unroll
+        for (int e = 0; e < 128; ++e)
+          r[e] = ((mw[e >> 5] >> (e & 31)) & 1u) ? r[e] : __float_as_uint(kNegInf);
+      }
+      float mx = kNegInf;
+#pragma unroll
+      for (int e = 0; e < 128; e += 2) mx = fmax3(mx, __uint_as_float(r[e]), __uint_as_float(r[e + 1]));
       const float m_new = fmaxf(m_run, mx);
-      const bool need = (m_new != -INFINITY) && (m_run == -INFINITY || m_new > m_run + kRescaleThreshold);
+      const bool need = (m_new != kNegInf) && (m_run == kNegInf || (m_new - m_run) * c > kRescaleThreshold);
       if (j > 0 && !(ok = mbar_wait(&bars.o_done, (j - 1) & 1, &abort_flag))) break;
       tc_fence_after();
       if (__any_sync(0xFFFFFFFFu, need)) {
-        const float alpha = (m_run == -INFINITY || m_new == -INFINITY) ? (m_run == -INFINITY ? 0.f : 1.f)
-                                                                        : fast_exp2(m_run - m_new);
+        const float alpha = m_run == kNegInf ? 0.f : (m_new == kNegInf ? 1.f : fast_exp2((m_run - m_new) * c));
         if (j > 0) {
 #pragma unroll
-          for (int c = 0; c < DH; c += 16) {
-            uint32_t r[16];
-            tmem_ld16(lane_base + kOCol + c, r);
+          for (int cc = 0; cc < DH; cc += 32) {
+            uint32_t o[32];
+            tmem_ld32(lane_base + kOCol + cc, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-            tmem_st16(lane_base + kOCol + c, r);
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(lane_base + kOCol + cc, o);
           }
           tmem_wait_st();
         }
-        l_run *= alpha;
-        if (m_new != -INFINITY) m_run = m_new;
+        l2.x *= alpha;
+        l2.y *= alpha;
+        if (m_new != kNegInf) m_run = m_new;
       }
-      const float m_use = m_run == -INFINITY ? 0.f : m_run;
-      // pass 2: p = exp2(s - m), row sum, P -> TMEM (bf16 pairs)
+      // p = exp2(c * (s - m)); masked entries hold -inf and give exactly 0
+      const float nmc = m_run == kNegInf ? 0.f : -m_run * c;
+      const float2 cc2 = make_float2(c, c);
+      const float2 nm2 = make_float2(nmc, nmc);
+      uint32_t pk[64];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(lane_base + kSCol + c * 32, r);
-        tmem_wait_ld();
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float s0 = __uint_as_float(r[e]) * scale_log2 - m_use;
-          const float s1 = __uint_as_float(r[e + 1]) * scale_log2 - m_use;
-          const float p0 = ((mw[c] >> e) & 1u) ? fast_exp2(s0) : 0.f;
-          const float p1 = ((mw[c] >> (e + 1)) & 1u) ? fast_exp2(s1) : 0.f;
-          l_run += p0 + p1;
-          pk[e / 2] = pack_bf16x2(p0, p1);
-        }
-        tmem_st16(lane_base + kPCol + c * 16, pk);
+      for (int e = 0; e < 128; e += 2) {
+        const float2 x = ffma2(make_float2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), cc2, nm2);
+        const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+        l2 = fadd2(l2, p);
+        pk[e >> 1] = pack_bf16x2(p.x, p.y);
+      }
+      {
+        uint32_t (&p0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&pk[0]);
+        uint32_t (&p1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&pk[32]);
+        tmem_st32(lane_base + kPCol, p0);
+        tmem_st32(lane_base + kPCol + 32, p1);
       }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars.p_full);
     }
+    const float l_run = l2.x + l2.y;
     // epilogue
     if (ok && n_tiles > 0 && mbar_wait(&bars.o_done, (n_tiles - 1) & 1, &abort_flag)) {
       tc_fence_after();
@@ -251,22 +264,23 @@ __global__ void __launch_bounds__(kThreads, 2)
       const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
       uint16_t* orow = out + ((size_t)bh * S + q) * DH;
 #pragma unroll
-      for (int c = 0; c < DH; c += 16) {
-        uint32_t r[16];
-        tmem_ld16(lane_base + kOCol + c, r);
+      for (int cc = 0; cc < DH; cc += 16) {
+        uint32_t o[16];
+        tmem_ld16(lane_base + kOCol + cc, o);
         tmem_wait_ld();
-        uint32_t pk[8];
+        uint32_t pko[8];
 #pragma unroll
         for (int e = 0; e < 16; e += 2)
-          pk[e / 2] = pack_bf16x2(__uint_as_float(r[e]) * inv_l, __uint_as_float(r[e + 1]) * inv_l);
+          pko[e / 2] = pack_bf16x2(__uint_as_float(o[e]) * inv_l, __uint_as_float(o[e + 1]) * inv_l);
         if (q < S) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c);
-          dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          uint4* dst = reinterpret_cast<uint4*>(orow + cc);
+          dst[0] = make_uint4(pko[0], pko[1], pko[2], pko[3]);
+          dst[1] = make_uint4(pko[4], pko[5], pko[6], pko[7]);
         }
       }
       if (q < S)
-        lse[(size_t)bh * S + q] = l_run > 0.f ? (m_run + __log2f(l_run)) * 0.6931471805599453f : -INFINITY;
+        lse[(size_t)bh * S + q] =
+            l_run > 0.f ? (m_run * c + __log2f(l_run)) * 0.6931471805599453f : -INFINITY;
     }
     tc_fence_before();
   }
