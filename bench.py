@@ -175,8 +175,8 @@ class Workload:
 
     def launches_per_step(self):
         # prepass: fk pack (feature / neighbor only), tile mask, tile list;
-        # forward: 1; backward: row stats, dK/dV, dQ
-        return sum((3 if k in (1, 2) else 2) + 1 + 3 for k in range(4))
+        # forward: main kernel + row fix-up; backward: row stats, dK/dV, dQ
+        return sum((3 if k in (1, 2) else 2) + 2 + 3 for k in range(4))
 
     def rebuild_plan(self, k):
         lib = self.rt._lib

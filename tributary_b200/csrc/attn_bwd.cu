@@ -19,7 +19,8 @@
 namespace rt {
 namespace bwd {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 576;         // producer, MMA, 16 softmax warps
+constexpr int kSoftmaxThreads = 512;  // four per TMEM lane quadrant, each owning 32 of a row's 128 columns
 constexpr int kTmemCols = 512;
 
 template <int DH>
@@ -65,36 +66,31 @@ __device__ __forceinline__ void init_barriers(Barriers& bars, int stages) {
   mbar_init(&bars.st_full[0], 1);
   mbar_init(&bars.st_full[1], 1);
   mbar_init(&bars.dp_full, 1);
-  mbar_init(&bars.pa_full, 128);
-  mbar_init(&bars.pb_full, 128);
+  mbar_init(&bars.pa_full, kSoftmaxThreads / 32);  // one arrival per softmax warp
+  mbar_init(&bars.pb_full, kSoftmaxThreads / 32);
   mbar_init(&bars.done, 1);
   mbar_init(&bars.drain, 1);
   fence_mbar_init();
 }
 
-// Softmax phase A for one 128x128 tile held in TMEM (one row per thread):
-// p = exp2(c * s + nl) with nl = -lse * log2(e), masked entries 0, packed as
-// bf16 pairs. `nl_col` (per column, from shared memory) is used when the
-// rows of the tile are keys (dK/dV), `nl_row` when they are queries (dQ).
+// Softmax phase A for a 32-column slice of one row of a 128x128 tile held in
+// TMEM (one row per thread): p = exp2(c * s + nl) with nl = -lse * log2(e),
+// masked entries 0, packed as 16 bf16 pairs. `nl_col` (per column, shared
+// memory) is used when the rows are keys (dK/dV), `nl_row` when they are
+// queries (dQ). `mw` is the mask word of these 32 columns.
 template <bool kPerColumn>
-__device__ __forceinline__ void softmax_phase_a(uint32_t taddr, bool full, const uint4& mk, float c,
-                                                const float* nl_col, float nl_row, uint32_t (&pk)[64]) {
-  uint32_t r[128];
-  {
-    uint32_t (&r0)[64] = *reinterpret_cast<uint32_t(*)[64]>(&r[0]);
-    uint32_t (&r1)[64] = *reinterpret_cast<uint32_t(*)[64]>(&r[64]);
-    tmem_ld64(taddr, r0);
-    tmem_ld64(taddr + 64, r1);
-  }
+__device__ __forceinline__ void softmax_phase_a(uint32_t taddr, bool full, uint32_t mw, float c,
+                                                const float* nl_col, float nl_row, uint32_t (&pk)[16]) {
+  uint32_t r[32];
+  tmem_ld32(taddr, r);
   tmem_wait_ld();
   if (!full) {
-    const uint32_t mw[4] = {mk.x, mk.y, mk.z, mk.w};
 #pragma unroll
-    for (int e = 0; e < 128; ++e) r[e] = ((mw[e >> 5] >> (e & 31)) & 1u) ? r[e] : __float_as_uint(-INFINITY);
+    for (int e = 0; e < 32; ++e) r[e] = ((mw >> e) & 1u) ? r[e] : __float_as_uint(-INFINITY);
   }
   const float2 c2 = make_float2(c, c);
 #pragma unroll
-  for (int e = 0; e < 128; e += 4) {
+  for (int e = 0; e < 32; e += 4) {
     float2 nl01, nl23;
     if (kPerColumn) {
       const float4 v = *reinterpret_cast<const float4*>(nl_col + e);
@@ -110,39 +106,46 @@ __device__ __forceinline__ void softmax_phase_a(uint32_t taddr, bool full, const
   }
 }
 
-// Softmax phase B: dS = P * (dP - delta) from the dP tile in TMEM, written
-// back as bf16 pairs into the first 64 columns of the same TMEM block (each
-// 32-column chunk is read before the 16 columns it lands on are written).
+// Softmax phase B for the same slice: dS = P * (dP - delta) from the 32 dP
+// columns at `taddr`, written back as 16 bf16 pairs over the first 16 of
+// those columns (read before written; slices of a row never overlap).
 template <bool kPerColumn>
-__device__ __forceinline__ void softmax_phase_b(uint32_t taddr, const uint32_t (&pk)[64], const float* nd_col,
+__device__ __forceinline__ void softmax_phase_b(uint32_t taddr, const uint32_t (&pk)[16], const float* nd_col,
                                                 float nd_row) {
+  uint32_t d[32];
+  tmem_ld32(taddr, d);
+  tmem_wait_ld();
+  uint32_t ds[16];
 #pragma unroll
-  for (int ch = 0; ch < 4; ++ch) {
-    uint32_t d[32];
-    tmem_ld32(taddr + ch * 32, d);
-    tmem_wait_ld();
-    uint32_t ds[16];
-#pragma unroll
-    for (int e = 0; e < 32; e += 4) {
-      float2 nd01, nd23;
-      if (kPerColumn) {
-        const float4 v = *reinterpret_cast<const float4*>(nd_col + ch * 32 + e);
-        nd01 = make_float2(v.x, v.y);
-        nd23 = make_float2(v.z, v.w);
-      } else {
-        nd01 = nd23 = make_float2(nd_row, nd_row);
-      }
-      const float2 g01 = fmul2(unpack_bf16x2(pk[ch * 16 + (e >> 1)]),
-                               fadd2(make_float2(__uint_as_float(d[e]), __uint_as_float(d[e + 1])), nd01));
-      const float2 g23 = fmul2(unpack_bf16x2(pk[ch * 16 + (e >> 1) + 1]),
-                               fadd2(make_float2(__uint_as_float(d[e + 2]), __uint_as_float(d[e + 3])), nd23));
-      ds[e >> 1] = pack_bf16x2(g01.x, g01.y);
-      ds[(e >> 1) + 1] = pack_bf16x2(g23.x, g23.y);
+  for (int e = 0; e < 32; e += 4) {
+    float2 nd01, nd23;
+    if (kPerColumn) {
+      const float4 v = *reinterpret_cast<const float4*>(nd_col + e);
+      nd01 = make_float2(v.x, v.y);
+      nd23 = make_float2(v.z, v.w);
+    } else {
+      nd01 = nd23 = make_float2(nd_row, nd_row);
     }
-    tmem_st16(taddr + ch * 16, ds);
+    const float2 g01 = fmul2(unpack_bf16x2(pk[e >> 1]),
+                             fadd2(make_float2(__uint_as_float(d[e]), __uint_as_float(d[e + 1])), nd01));
+    const float2 g23 = fmul2(unpack_bf16x2(pk[(e >> 1) + 1]),
+                             fadd2(make_float2(__uint_as_float(d[e + 2]), __uint_as_float(d[e + 3])), nd23));
+    ds[e >> 1] = pack_bf16x2(g01.x, g01.y);
+    ds[(e >> 1) + 1] = pack_bf16x2(g23.x, g23.y);
   }
+  tmem_st16(taddr, ds);
 }
 
+// TMEM column of the bf16 P / dS operand for MMA k-step ks (16 rows of the
+// reduction dimension): column group g = ks / 2 keeps its 32 entries packed
+// in columns [32g, 32g + 16).
+__device__ __forceinline__ uint32_t packed_col(int ks) { return (uint32_t)((ks >> 1) * 32 + (ks & 1) * 8); }
+
+// Epilogue slice of the DH output columns handled by column group g.
+template <int DH>
+struct EpiSlice {
+  static constexpr int kCols = DH / 4 < 16 ? 16 : DH / 4;
+};
 
 // Row statistics for the gradient kernels, padded to whole tiles and stored
 // negated so they enter the exponent / difference as FMA addends:
@@ -194,7 +197,9 @@ __device__ __forceinline__ void store_row_bf16(uint16_t* dst, const uint32_t (&p
 // ---------------------------------------------------------------------------
 // dQ: one CTA per (b, h, q-tile); thread = query row.
 // TMEM: S0 [0,128), S1 [128,256) fp32 (double buffered), dP [256,384) fp32
-// with dS written over its first 64 columns as bf16 pairs, dQ [384,384+DH).
+// with dS written as bf16 pairs over columns [32g, 32g+16) of it (one run per
+// 32-column slice g), dQ [384,384+DH). Sixteen softmax warps: four per TMEM
+// lane quadrant, each owning 32 of the 128 columns.
 // Per k-tile j: the MMA thread issues S_{j+1} as soon as softmax phase A has
 // read S_j, so QK^T overlaps phase B; dP_{j+1} follows dQ += dS_j K_j and
 // overlaps the next phase A.
@@ -297,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < RT_TILE / 16; ++ks)
-          mma_ts(tmem + kDQ, tmem + kDP + ks * 8,
+          mma_ts(tmem + kDQ, tmem + kDP + packed_col(ks),
                  sdesc(k_addr(j) + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_q,
                  (j > 0 || ks > 0) ? 1u : 0u);
         mma_commit(&bars.ring_empty[j % C::kStages]);
@@ -310,50 +315,50 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     const int quad = warp & 3;
+    const int grp = (warp - 2) >> 2;  // column group: columns [32 grp, 32 grp + 32) of every tile
     const int row = quad * 32 + lane;
     const int q = qt * RT_TILE + row;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
-    const uint32_t* masks = plan.tile_masks + ((size_t)row_list * T) * RT_TILE * 4;
+    const uint32_t col0 = (uint32_t)(grp * 32);
+    const uint32_t* masks = plan.tile_masks + ((size_t)row_list * T) * RT_TILE * 4 + grp;
     const int Sp = T * RT_TILE;
     const float nl = stats[(size_t)bh * 2 * Sp + q];
     const float nd = stats[(size_t)bh * 2 * Sp + Sp + q];
     auto load_mask = [&](int ent) {
-      uint4 mk = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
-      if (ent >= 0) mk = __ldg(reinterpret_cast<const uint4*>(masks + ((size_t)(ent & 0x7FFFFFFF) * RT_TILE + row) * 4));
-      return mk;
+      return ent >= 0 ? __ldg(masks + ((size_t)(ent & 0x7FFFFFFF) * RT_TILE + row) * 4) : 0xFFFFFFFFu;
     };
-    uint4 mk_next = n_tiles > 0 ? load_mask(s_list[0]) : make_uint4(0u, 0u, 0u, 0u);
+    uint32_t mk_next = n_tiles > 0 ? load_mask(s_list[0]) : 0u;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const bool full = s_list[j] < 0;
-      const uint4 mk = mk_next;
+      const uint32_t mk = mk_next;
       if (j + 1 < n_tiles) mk_next = load_mask(s_list[j + 1]);
       if (!(ok = mbar_wait(&bars.st_full[j & 1], (j >> 1) & 1, &abort_flag))) break;
       tc_fence_after();
-      uint32_t pk[64];
-      softmax_phase_a<false>(lane_base + kS0 + (j & 1) * 128, full, mk, scale_log2, nullptr, nl, pk);
+      uint32_t pk[16];
+      softmax_phase_a<false>(lane_base + kS0 + (j & 1) * 128 + col0, full, mk, scale_log2, nullptr, nl, pk);
       tc_fence_before();
-      mbar_arrive(&bars.pa_full);
+      mbar_arrive_warp(&bars.pa_full);
       if (!(ok = mbar_wait(&bars.dp_full, j & 1, &abort_flag))) break;
       tc_fence_after();
-      softmax_phase_b<false>(lane_base + kDP, pk, nullptr, nd);
+      softmax_phase_b<false>(lane_base + kDP + col0, pk, nullptr, nd);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bars.pb_full);
+      mbar_arrive_warp(&bars.pb_full);
     }
     if (ok && n_tiles > 0 && mbar_wait(&bars.done, 0, &abort_flag)) {
       tc_fence_after();
       uint16_t* dst = dq + ((size_t)bh * S + q) * DH;
 #pragma unroll
-      for (int c = 0; c < DH; c += 16) {
+      for (int c = grp * EpiSlice<DH>::kCols; c < (grp + 1) * EpiSlice<DH>::kCols && c < DH; c += 16) {
         uint32_t r[16];
         tmem_ld16(lane_base + kDQ + c, r);
         tmem_wait_ld();
-        uint32_t pk[8];
+        uint32_t pko[8];
 #pragma unroll
         for (int e = 0; e < 16; e += 2)
-          pk[e / 2] = pack_bf16x2(__uint_as_float(r[e]) * scale, __uint_as_float(r[e + 1]) * scale);
-        if (q < S) store_row_bf16(dst + c, pk);
+          pko[e / 2] = pack_bf16x2(__uint_as_float(r[e]) * scale, __uint_as_float(r[e + 1]) * scale);
+        if (q < S) store_row_bf16(dst + c, pko);
       }
     }
     tc_fence_before();
@@ -367,9 +372,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---------------------------------------------------------------------------
 // dK, dV: one CTA per (b, h, k-tile); thread = key row.
-// TMEM: S^T0 [0,128), S^T1 [128,256) fp32 (double buffered; P^T overwrites the
-// first 64 columns as bf16 pairs), dP^T [256,384) fp32 (dS^T overwrites its
-// first 64 columns), dV [384,384+DH), dK [384+DH,384+2DH).
+// TMEM: S^T0 [0,128), S^T1 [128,256) fp32 (double buffered; P^T overwrites
+// columns [32g, 32g+16) as bf16 pairs, one run per 32-column slice g), dP^T
+// [256,384) fp32 (dS^T likewise), dV [384,384+DH), dK [384+DH,384+2DH).
+// Sixteen softmax warps: four per TMEM lane quadrant, each owning 32 columns.
 // Per q-tile i: dV_i and S^T_{i+1} follow softmax phase A (overlapping phase
 // B), dK_i and dP^T_{i+1} follow phase B (overlapping the next phase A).
 // ---------------------------------------------------------------------------
@@ -468,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < RT_TILE / 16; ++ks)  // dV += P^T_i dO_i
-          mma_ts(tmem + kDV, tmem + kST0 + (i & 1) * 128 + ks * 8,
+          mma_ts(tmem + kDV, tmem + kST0 + (i & 1) * 128 + packed_col(ks),
                  sdesc(do_addr(i) + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_g,
                  (i > 0 || ks > 0) ? 1u : 0u);
         if (i + 1 < n_tiles) {
@@ -481,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < RT_TILE / 16; ++ks)  // dK += dS^T_i Q_i
-          mma_ts(tmem + kDK, tmem + kDPT + ks * 8,
+          mma_ts(tmem + kDK, tmem + kDPT + packed_col(ks),
                  sdesc(q_addr(i) + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_g,
                  (i > 0 || ks > 0) ? 1u : 0u);
         mma_commit(&bars.ring_empty[i % C::kStages]);
@@ -494,65 +500,59 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     const int quad = warp & 3;
+    const int grp = (warp - 2) >> 2;  // column group: queries [32 grp, 32 grp + 32) of every tile
     const int row = quad * 32 + lane;  // key within the tile
     const int key = kt * RT_TILE + row;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
-    const uint32_t* masks_t = plan.tile_masks_t + ((size_t)col_list * T) * RT_TILE * 4;
+    const uint32_t col0 = (uint32_t)(grp * 32);
+    const uint32_t* masks_t = plan.tile_masks_t + ((size_t)col_list * T) * RT_TILE * 4 + grp;
     auto load_mask = [&](int ent) {
-      uint4 mk = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
-      if (ent >= 0)
-        mk = __ldg(reinterpret_cast<const uint4*>(masks_t + ((size_t)(ent & 0x7FFFFFFF) * RT_TILE + row) * 4));
-      return mk;
+      return ent >= 0 ? __ldg(masks_t + ((size_t)(ent & 0x7FFFFFFF) * RT_TILE + row) * 4) : 0xFFFFFFFFu;
     };
-    uint4 mk_next = n_tiles > 0 ? load_mask(s_list[0]) : make_uint4(0u, 0u, 0u, 0u);
+    uint32_t mk_next = n_tiles > 0 ? load_mask(s_list[0]) : 0u;
     bool ok = true;
     for (int i = 0; i < n_tiles; ++i) {
       const bool full = s_list[i] < 0;
-      const uint4 mk = mk_next;
+      const uint32_t mk = mk_next;
       if (i + 1 < n_tiles) mk_next = load_mask(s_list[i + 1]);
       const int stage = i % C::kStages;
       if (!(ok = mbar_wait(&bars.ring_full[stage], (i / C::kStages) & 1, &abort_flag))) break;
-      const float* nl = reinterpret_cast<const float*>(smem + C::kRL + stage * C::kRowStatBytes);
+      const float* nl = reinterpret_cast<const float*>(smem + C::kRL + stage * C::kRowStatBytes) + col0;
       const float* nd = nl + RT_TILE;
       if (!(ok = mbar_wait(&bars.st_full[i & 1], (i >> 1) & 1, &abort_flag))) break;
       tc_fence_after();
-      uint32_t pk[64];
-      const uint32_t st_addr = lane_base + kST0 + (i & 1) * 128;
+      uint32_t pk[16];
+      const uint32_t st_addr = lane_base + kST0 + (i & 1) * 128 + col0;
       softmax_phase_a<true>(st_addr, full, mk, scale_log2, nl, 0.f, pk);
-      {
-        uint32_t (&p0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&pk[0]);
-        uint32_t (&p1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&pk[32]);
-        tmem_st32(st_addr, p0);  // P^T over the first 64 columns of its S^T buffer
-        tmem_st32(st_addr + 32, p1);
-      }
+      tmem_st16(st_addr, pk);  // P^T over the first 16 columns of this slice
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bars.pa_full);
+      mbar_arrive_warp(&bars.pa_full);
       if (!(ok = mbar_wait(&bars.dp_full, i & 1, &abort_flag))) break;
       tc_fence_after();
-      softmax_phase_b<true>(lane_base + kDPT, pk, nd, 0.f);
+      softmax_phase_b<true>(lane_base + kDPT + col0, pk, nd, 0.f);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bars.pb_full);
+      mbar_arrive_warp(&bars.pb_full);
     }
     if (ok && n_tiles > 0 && mbar_wait(&bars.done, 0, &abort_flag)) {
       tc_fence_after();
       uint16_t* dst_v = dv + ((size_t)bh * S + key) * DH;
       uint16_t* dst_k = dk + ((size_t)bh * S + key) * DH;
 #pragma unroll
-      for (int c = 0; c < DH; c += 16) {
-        uint32_t r[16], pk[8];
+      for (int c = grp * EpiSlice<DH>::kCols; c < (grp + 1) * EpiSlice<DH>::kCols && c < DH; c += 16) {
+        uint32_t r[16], pko[8];
         tmem_ld16(lane_base + kDV + c, r);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 16; e += 2) pk[e / 2] = pack_bf16x2(__uint_as_float(r[e]), __uint_as_float(r[e + 1]));
-        if (key < S) store_row_bf16(dst_v + c, pk);
+        for (int e = 0; e < 16; e += 2) pko[e / 2] = pack_bf16x2(__uint_as_float(r[e]), __uint_as_float(r[e + 1]));
+        if (key < S) store_row_bf16(dst_v + c, pko);
         tmem_ld16(lane_base + kDK + c, r);
         tmem_wait_ld();
 #pragma unroll
         for (int e = 0; e < 16; e += 2)
-          pk[e / 2] = pack_bf16x2(__uint_as_float(r[e]) * scale, __uint_as_float(r[e + 1]) * scale);
-        if (key < S) store_row_bf16(dst_k + c, pk);
+          pko[e / 2] = pack_bf16x2(__uint_as_float(r[e]) * scale, __uint_as_float(r[e + 1]) * scale);
+        if (key < S) store_row_bf16(dst_k + c, pko);
       }
     }
     tc_fence_before();

@@ -1,101 +1,272 @@
 // Forward masked attention on sm_100a (tcgen05 + TMA), one 128-query tile of
-// one (batch, head) per CTA, iterating only the live key tiles of the plan.
+// one (batch, head) per CTA, iterating only the live key tiles of the plan
+// (attn_fwd_kernel), followed by an exact fp32 fix-up of the rare rows it
+// marks (attn_fwd_rowfix_kernel).
 //
 // Replaces confluence/confluence/layers.py:83-94: s = q k^T * scale,
 // where(mask, s, -1e9), softmax, p v. Masked elements are excluded exactly
 // (every row keeps its diagonal, so the reference's -1e9 entries contribute
 // exp(-1e9 - max) == 0 in fp32). Also writes lse = ln sum_j exp(s_ij).
 //
-// Warp roles (192 threads):
-//   warp 0      TMA producer (Q once, K/V ring) + TMEM allocation
-//   warp 1      MMA issuer (one thread): S = Q K^T, O += P V
-//   warps 2..5  softmax: thread = query row (TMEM lane), online softmax in
-//               fp32 (log2 domain), lazy O rescale, P -> TMEM as bf16,
-//               epilogue O / l -> bf16, lse.
-// Tensor memory (256 columns): S [0,128) fp32, P [128,192) bf16x2, O [192,192+DH).
-// Per-tile mask bits come from the prepass (query-major words); fully-live
-// tiles skip the mask entirely.
+// The main kernel's structure (warp roles, TMEM layout, exponent reference)
+// is described above attn_fwd_kernel.
+#include <algorithm>
+
 #include "rt_device.cuh"
 #include "rt_internal.h"
 
 namespace rt {
 namespace fwd {
 
-constexpr int kThreads = 192;
-constexpr int kSCol = 0;
-constexpr int kPCol = 128;
-constexpr int kOCol = 192;
-constexpr int kTmemCols = 256;
-constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by 2^8
+// Exponent reference offset (log2 units): p = exp2(c (s - s_ii) - kRefShift).
+// The row's largest term is >= 2^-kRefShift, far above the fp32 / bf16
+// normal range limit; rows whose terms grow past 2^100 go to the exact path.
+constexpr float kRefShift = 64.0f;
 constexpr int kMaxTiles = 65536 / RT_TILE;  // tiles per row of the plan (seq_len <= 65536)
+static_assert(kMaxTiles <= 512, "tile list must fit in shared memory");
+
+// ---------------------------------------------------------------------------
+// Exact fallback for the rare rows the main kernel marks (lse = NaN): their
+// logit spread exceeded the range of the diagonal reference. One warp per
+// marked row recomputes it in fp32 on the CUDA cores with an online max:
+// lanes take 32 keys at a time, o is spread over the lanes (DH/32 columns
+// each). In the common case no row is marked and the kernel only scans lse.
+// ---------------------------------------------------------------------------
+template <int DH>
+__global__ void __launch_bounds__(256) attn_fwd_rowfix_kernel(const uint16_t* __restrict__ qg,
+                                                              const uint16_t* __restrict__ kg,
+                                                              const uint16_t* __restrict__ vg, const rt_tile_plan plan,
+                                                              int H, int S, float c, uint16_t* __restrict__ out,
+                                                              float* __restrict__ lse) {
+  constexpr int kPer = DH / 32;  // output columns per lane
+  const int lane = threadIdx.x & 31;
+  const long long total = (long long)plan.batch * H * S;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  const int T = plan.tiles;
+  for (long long base = ((long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32; base < total;
+       base += warps * 32) {
+    const long long mine = base + lane;
+    uint32_t todo = __ballot_sync(0xFFFFFFFFu, mine < total && isnan(lse[mine]));
+    while (todo) {
+      const int src = __ffs(todo) - 1;
+      todo &= todo - 1;
+      const long long r = base + src;
+      const int bh = (int)(r / S), i = (int)(r % S);
+      const int b = bh / H, qt = i / RT_TILE, ri = i % RT_TILE;
+      float qf[DH];
+#pragma unroll
+      for (int d = 0; d < DH; d += 2) {
+        const float2 f = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(qg + (size_t)r * DH + d));
+        qf[d] = f.x;
+        qf[d + 1] = f.y;
+      }
+      float m = -INFINITY, l = 0.f, o[kPer];
+#pragma unroll
+      for (int e = 0; e < kPer; ++e) o[e] = 0.f;
+      const int lb = plan.q2k_ptr[b * T + qt], le = plan.q2k_ptr[b * T + qt + 1];
+      for (int t = lb; t < le; ++t) {
+        const int ent = plan.q2k_idx[t];
+        const int kt = ent & 0x7FFFFFFF;
+        const uint32_t* mrow = plan.tile_masks + ((((size_t)b * T + qt) * T + kt) * RT_TILE + ri) * 4;
+        for (int ch = 0; ch < 4; ++ch) {
+          const int j = kt * RT_TILE + ch * 32 + lane;
+          const bool live = j < S && (ent < 0 || ((mrow[ch] >> lane) & 1u));
+          float sc = -INFINITY;
+          if (live) {
+            float acc = 0.f;
+            const uint16_t* krow = kg + ((size_t)bh * S + j) * DH;
+#pragma unroll
+            for (int d = 0; d < DH; d += 2) {
+              const float2 kf = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(krow + d));
+              acc = fmaf(qf[d], kf.x, fmaf(qf[d + 1], kf.y, acc));
+            }
+            sc = acc * c;
+          }
+          float cm = sc;
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xFFFFFFFFu, cm, off));
+          const float mn = fmaxf(m, cm);
+          if (mn == -INFINITY) continue;
+          const float alpha = m == -INFINITY ? 0.f : exp2f(m - mn);
+          const float p = live ? exp2f(sc - mn) : 0.f;
+          float ps = p;
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xFFFFFFFFu, ps, off);
+          l = l * alpha + ps;
+#pragma unroll
+          for (int e = 0; e < kPer; ++e) o[e] *= alpha;
+          for (int src2 = 0; src2 < 32; ++src2) {
+            const float pj = __shfl_sync(0xFFFFFFFFu, p, src2);
+            const int jj = kt * RT_TILE + ch * 32 + src2;
+            if (pj != 0.f) {
+              const uint16_t* vrow = vg + ((size_t)bh * S + jj) * DH + lane * kPer;
+#pragma unroll
+              for (int e = 0; e < kPer; ++e) o[e] = fmaf(pj, __uint_as_float((uint32_t)vrow[e] << 16), o[e]);
+            }
+          }
+          m = mn;
+        }
+      }
+      const float inv_l = l > 0.f ? 1.f / l : 0.f;
+      uint16_t* orow = out + (size_t)r * DH + lane * kPer;
+#pragma unroll
+      for (int e = 0; e < kPer; ++e) {
+        const __nv_bfloat16 bv = __float2bfloat16_rn(o[e] * inv_l);
+        orow[e] = *reinterpret_cast<const uint16_t*>(&bv);
+      }
+      if (lane == 0) lse[r] = l > 0.f ? (m + log2f(l)) * 0.6931471805599453f : -INFINITY;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Main forward kernel: persistent, one CTA per SM, looping over work items
+// (b, h, q-tile) c, c + G, c + 2G, ... (G = grid size) as one global sequence
+// of live tiles, so the next item's loads and prologue overlap the current
+// item's work and the epilogue overlaps the next item.
+//   warp 0       producer: per tile, a tile-info word into a small ring, the
+//                K / V tiles (TMA) and, for partial tiles, the 2 KB block of
+//                mask words (bulk copy) into a 4-stage ring; per item, Q into
+//                one of two slots
+//   warp 1       MMA issuer: S_g = Q K_g^T into S buffer g % 3, O += P_g V_g
+//                into the item's O buffer (two, alternating by item)
+//   warps 2..5   epilogue warpgroup: diagonal logits two items ahead, then
+//                O / l -> bf16 and lse per item
+//   warps 6..17  softmax: three sets of 4 warps (one per TMEM lane quadrant);
+//                set s takes the global tiles g with g % 3 == s; thread =
+//                query row, the row's 128 columns in four 32-column chunks
+// Exponent reference: each row uses its own diagonal logit s_ii = q_i . k_i
+// (always live), p = exp2(c (s - s_ii) - kRefShift): the largest term is at
+// least 2^-kRefShift, so nothing that matters underflows, and no online max
+// or O rescaling is needed (softmax is invariant to the reference). A row
+// whose terms leave the safe range (row sum >= 2^100 or |O| >= 2^120, i.e. a
+// logit spread above about (100 + kRefShift)/c, impossible for L2-normalised
+// q, k) is marked with lse = NaN and recomputed by attn_fwd_rowfix_kernel.
+// TMEM (512 columns): S buffers [0,128), [128,256), [256,384) fp32 with P_g
+// written as bf16 pairs over columns [0,64) of its buffer, O buffers
+// [384, 384+DH) and [384+DH, 384+2DH).
+// ---------------------------------------------------------------------------
+constexpr int kSets = 3;
+constexpr int kSetWarps = 4;
+constexpr int kSoftmaxWarps = kSets * kSetWarps;
+constexpr int kEpiWarps = 4;
+constexpr int kMainThreads = 32 * (2 + kEpiWarps + kSoftmaxWarps);
+constexpr int kMainTmemCols = 512;
+constexpr int kOMain = kSets * 128;
+constexpr int kStages = 4;
+constexpr int kInfoRing = 8;
+constexpr int kMaskBytes = RT_TILE * 16;
+// tile-info word: kt (bits 0-15), fully live (16), first tile of its item (17),
+// last tile of its item (18)
+constexpr uint32_t kInfoFull = 1u << 16, kInfoFirst = 1u << 17, kInfoLast = 1u << 18;
 
 template <int DH>
-struct Cfg {
+struct MainCfg {
   static constexpr int kRowBytes = DH * 2;
   static constexpr int kTileBytes = RT_TILE * kRowBytes;
   static constexpr uint32_t kSwizzle = DH == 64 ? SW_128B : SW_64B;
   static constexpr int kSBO = 8 * kRowBytes;
-  static constexpr int kStages = DH == 64 ? 2 : 4;
-  static constexpr int kQOff = 0;
-  static constexpr int kKOff = kTileBytes;
-  static constexpr int kVOff = kKOff + kStages * kTileBytes;
-  static constexpr int kSmemBytes = kVOff + kStages * kTileBytes;
-  // 256 TMEM columns per CTA: at most two CTAs may share an SM, so ask for
-  // enough shared memory that a third never lands there.
-  static constexpr int kDynSmem = (kSmemBytes + 1024) > 78 * 1024 ? (kSmemBytes + 1024) : 78 * 1024;
+  static constexpr int kQOff = 0;                                  // two Q slots
+  static constexpr int kKOff = 2 * kTileBytes;                     // K ring
+  static constexpr int kVOff = kKOff + kStages * kTileBytes;       // V ring
+  static constexpr int kMOff = kVOff + kStages * kTileBytes;       // mask ring
+  static constexpr int kSmemBytes = kMOff + kStages * kMaskBytes;
+  static constexpr int kDynSmem = kSmemBytes + 1024;
 };
 
-struct __align__(8) Barriers {
-  uint64_t q_full;
-  uint64_t kv_full[4];
-  uint64_t kv_empty[4];
-  uint64_t s_full;
-  uint64_t p_full;
-  uint64_t o_done;
+struct __align__(8) MainBarriers {
+  uint64_t q_full[2], q_empty[2];
+  uint64_t kv_full[kStages], kv_empty[kStages];
+  uint64_t st_full[kSets], p_full[kSets], o_done[kSets];
+  uint64_t item_done[2], o_free[2];
+  uint64_t sdiag_full[2], lsum_full[2];
   uint64_t drain;
 };
 
+struct ItemCoord {
+  int b, h, qt;
+};
+__device__ __forceinline__ ItemCoord item_coord(int item, int H, int T) {
+  ItemCoord c;
+  c.qt = item % T;
+  const int bh = item / T;
+  c.h = bh % H;
+  c.b = bh / H;
+  return c;
+}
+
 template <int DH>
-__global__ void __launch_bounds__(kThreads, 2)
+__device__ __forceinline__ float diag_logit(const uint16_t* __restrict__ qg, const uint16_t* __restrict__ kg,
+                                            size_t row) {
+  const uint4* qa = reinterpret_cast<const uint4*>(qg + row * DH);
+  const uint4* ka = reinterpret_cast<const uint4*>(kg + row * DH);
+  float sd = 0.f;
+#pragma unroll
+  for (int v = 0; v < DH / 8; ++v) {
+    const uint4 a = __ldg(qa + v), kk = __ldg(ka + v);
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, kw[4] = {kk.x, kk.y, kk.z, kk.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 af = unpack_bf16x2(aw[e]), kf = unpack_bf16x2(kw[e]);
+      sd = fmaf(af.x, kf.x, fmaf(af.y, kf.y, sd));
+    }
+  }
+  return sd;
+}
+
+template <int DH>
+__global__ void __launch_bounds__(kMainThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                    const __grid_constant__ CUtensorMap tm_v, const rt_tile_plan plan, int H, int S,
-                    float scale_log2, uint16_t* __restrict__ out, float* __restrict__ lse) {
-  using C = Cfg<DH>;
+                    const __grid_constant__ CUtensorMap tm_v, const uint16_t* __restrict__ qg,
+                    const uint16_t* __restrict__ kg, const rt_tile_plan plan, int H, int S, float scale_log2,
+                    uint16_t* __restrict__ out, float* __restrict__ lse) {
+  using C = MainCfg<DH>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ Barriers bars;
+  __shared__ MainBarriers bars;
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_flag;
-  __shared__ int s_list[kMaxTiles];
+  __shared__ uint32_t s_info[kInfoRing];
+  __shared__ float s_sdiag[2][RT_TILE];
+  __shared__ float s_lpart[2][kSets][RT_TILE];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int qt = blockIdx.x;
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
   const int T = plan.tiles;
-  const int bh = b * H + h;
-  const int row_list = b * T + qt;
-  const int list_begin = plan.q2k_ptr[row_list];
-  const int n_tiles = plan.q2k_ptr[row_list + 1] - list_begin;
-  const int* list = plan.q2k_idx + list_begin;
-  for (int i = threadIdx.x; i < n_tiles; i += kThreads) s_list[i] = list[i];
+  const int n_items_total = plan.batch * H * T;
+  const int G = gridDim.x;
+  const int n_items = (n_items_total - (int)blockIdx.x + G - 1) / G;  // items of this CTA
+  auto item_id = [&](int k) { return (int)blockIdx.x + k * G; };
+  auto item_ntiles = [&](int item) {
+    const ItemCoord ic = item_coord(item, H, T);
+    const int r = ic.b * T + ic.qt;
+    return plan.q2k_ptr[r + 1] - plan.q2k_ptr[r];
+  };
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
-    mbar_init(&bars.q_full, 1);
-    for (int s = 0; s < C::kStages; ++s) {
-      mbar_init(&bars.kv_full[s], 1);
-      mbar_init(&bars.kv_empty[s], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars.q_full[i], 1);
+      mbar_init(&bars.q_empty[i], 1);
+      mbar_init(&bars.item_done[i], 1);
+      mbar_init(&bars.o_free[i], kEpiWarps);
+      mbar_init(&bars.sdiag_full[i], kEpiWarps);
+      mbar_init(&bars.lsum_full[i], kSoftmaxWarps);
     }
-    mbar_init(&bars.s_full, 1);
-    mbar_init(&bars.p_full, 128);
-    mbar_init(&bars.o_done, 1);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&bars.kv_full[i], 1);
+      mbar_init(&bars.kv_empty[i], 1);
+    }
+    for (int i = 0; i < kSets; ++i) {
+      mbar_init(&bars.st_full[i], 1);
+      mbar_init(&bars.p_full[i], kSetWarps);
+      mbar_init(&bars.o_done[i], 1);
+    }
     mbar_init(&bars.drain, 1);
     fence_mbar_init();
   }
   if (warp == 0) {
-    tmem_alloc(&tmem_base_s, kTmemCols);
+    tmem_alloc(&tmem_base_s, kMainTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -104,183 +275,262 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t tmem = tmem_base_s;
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0 && n_tiles > 0) {
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(&bars.q_full, C::kTileBytes);
-      tma_load_3d(smem + C::kQOff, &tm_q, &bars.q_full, 0, qt * RT_TILE, bh);
-      int j = 0;
-      for (; j < n_tiles; ++j) {
-        const int s = j % C::kStages;
-        if (j >= C::kStages && !mbar_wait(&bars.kv_empty[s], ((j / C::kStages) - 1) & 1, &abort_flag)) break;
-        const int kt = s_list[j] & 0x7FFFFFFF;
-        mbar_arrive_expect_tx(&bars.kv_full[s], 2 * C::kTileBytes);
-        tma_load_3d(smem + C::kKOff + s * C::kTileBytes, &tm_k, &bars.kv_full[s], 0, kt * RT_TILE, bh);
-        tma_load_3d(smem + C::kVOff + s * C::kTileBytes, &tm_v, &bars.kv_full[s], 0, kt * RT_TILE, bh);
+    // ---------------- producer ----------------
+    // item k's row pointer and first 32 list entries are loaded while item
+    // k-1 streams, so item boundaries cost no L2 round trip
+    auto item_list = [&](int k, int& lb, int& n, int& ent0) {
+      lb = 0;
+      n = 0;
+      ent0 = 0;
+      if (k >= n_items) return;
+      const ItemCoord ic = item_coord(item_id(k), H, T);
+      const int r = ic.b * T + ic.qt;
+      lb = __ldg(plan.q2k_ptr + r);
+      n = __ldg(plan.q2k_ptr + r + 1) - lb;
+      ent0 = lane < n ? __ldg(plan.q2k_idx + lb + lane) : 0;
+    };
+    int g = 0;   // global tile index
+    int kq = 0;  // Q loads issued
+    bool ok = true;
+    int lb_next, n_next, ent_next;
+    item_list(0, lb_next, n_next, ent_next);
+    for (int k = 0; ok && k < n_items; ++k) {
+      const int lb = lb_next, n = n_next;
+      int ent_l = ent_next;
+      item_list(k + 1, lb_next, n_next, ent_next);
+      const ItemCoord ic = item_coord(item_id(k), H, T);
+      const int bh = ic.b * H + ic.h;
+      const int r = ic.b * T + ic.qt;
+      if (k >= 2 && !(ok = mbar_wait_warp(&bars.q_empty[k & 1], ((k - 2) >> 1) & 1, &abort_flag))) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&bars.q_full[k & 1], C::kTileBytes);
+        tma_load_3d(smem + C::kQOff + (k & 1) * C::kTileBytes, &tm_q, &bars.q_full[k & 1], 0, ic.qt * RT_TILE, bh);
       }
-      // Drain: every load issued must land before the CTA may exit.
-      for (int jj = max(0, j - C::kStages); jj < j; ++jj) {
-        const int s = jj % C::kStages;
-        volatile int no_abort = 0;
-        mbar_wait(&bars.kv_full[s], (jj / C::kStages) & 1, &no_abort);
+      kq = k + 1;
+      const uint32_t* mask_base = plan.tile_masks + (size_t)r * T * RT_TILE * 4;
+      for (int t0 = 0; ok && t0 < n; t0 += 32) {
+        if (t0 > 0) ent_l = (t0 + lane < n) ? __ldg(plan.q2k_idx + lb + t0 + lane) : 0;
+        const int cnt = min(32, n - t0);
+        for (int tt = 0; tt < cnt; ++tt, ++g) {
+          const int ent = __shfl_sync(0xFFFFFFFFu, ent_l, tt);
+          const int t = t0 + tt;
+          const int st = g % kStages;
+          if (g >= kStages && !(ok = mbar_wait_warp(&bars.kv_empty[st], ((g / kStages) - 1) & 1, &abort_flag))) break;
+          if (lane == 0) {
+            const int kt = ent & 0x7FFFFFFF;
+            const bool full = ent < 0;
+            s_info[g % kInfoRing] = (uint32_t)kt | (full ? kInfoFull : 0u) | (t == 0 ? kInfoFirst : 0u) |
+                                    (t == n - 1 ? kInfoLast : 0u);
+            mbar_arrive_expect_tx(&bars.kv_full[st], 2 * C::kTileBytes + (full ? 0 : kMaskBytes));
+            tma_load_3d(smem + C::kKOff + st * C::kTileBytes, &tm_k, &bars.kv_full[st], 0, kt * RT_TILE, bh);
+            tma_load_3d(smem + C::kVOff + st * C::kTileBytes, &tm_v, &bars.kv_full[st], 0, kt * RT_TILE, bh);
+            if (!full)
+              bulk_load(smem + C::kMOff + st * kMaskBytes, mask_base + (size_t)kt * RT_TILE * 4, kMaskBytes,
+                        &bars.kv_full[st]);
+          }
+          __syncwarp();
+        }
       }
-      volatile int no_abort = 0;
-      mbar_wait(&bars.q_full, 0, &no_abort);
     }
+    // drain: every load issued must land before the CTA exits
+    volatile int no_abort = 0;
+    for (int gg = max(0, g - kStages); gg < g; ++gg)
+      mbar_wait(&bars.kv_full[gg % kStages], (gg / kStages) & 1, &no_abort);
+    for (int kk = max(0, kq - 2); kk < kq; ++kk) mbar_wait(&bars.q_full[kk & 1], (kk >> 1) & 1, &no_abort);
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0 && n_tiles > 0) {
+    if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, DH, false, true);
-      const uint32_t q_addr = smem_u32(smem + C::kQOff);
-      bool ok = mbar_wait(&bars.q_full, 0, &abort_flag);
-      tc_fence_after();
-      for (int j = 0; ok && j <= n_tiles; ++j) {
-        if (j > 0) {
-          // O += P_{j-1} V_{j-1}
-          if (!(ok = mbar_wait(&bars.p_full, (j - 1) & 1, &abort_flag))) break;
-          tc_fence_after();
-          const int sp = (j - 1) % C::kStages;
-          const uint32_t v_addr = smem_u32(smem + C::kVOff + sp * C::kTileBytes);
-#pragma unroll
-          for (int ks = 0; ks < RT_TILE / 16; ++ks) {
-            const uint64_t bdesc = sdesc(v_addr + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle);
-            mma_ts(tmem + kOCol, tmem + kPCol + ks * 8, bdesc, idesc_o, (j > 1 || ks > 0) ? 1u : 0u);
-          }
-          mma_commit(&bars.o_done);
-          mma_commit(&bars.kv_empty[sp]);
+      bool ok = true;
+      // S cursor: item kS, tile tS within it, global gS (next item's count prefetched)
+      int kS = 0, tS = 0, gS = 0;
+      int nS = n_items > 0 ? item_ntiles(item_id(0)) : 0;
+      int nS_next = n_items > 1 ? item_ntiles(item_id(1)) : 0;
+      auto issue_next_s = [&]() -> bool {  // issues S_gS, advances the cursor; false when done
+        while (kS < n_items && tS >= nS) {  // leave finished (or empty) items, releasing their Q slot
+          if (nS == 0 && !(ok = mbar_wait(&bars.q_full[kS & 1], (kS >> 1) & 1, &abort_flag))) return false;
+          mma_commit(&bars.q_empty[kS & 1]);
+          ++kS;
+          tS = 0;
+          nS = nS_next;
+          nS_next = kS + 1 < n_items ? item_ntiles(item_id(kS + 1)) : 0;
         }
-        if (j < n_tiles) {
-          // S = Q K_j^T
-          const int s = j % C::kStages;
-          if (!(ok = mbar_wait(&bars.kv_full[s], (j / C::kStages) & 1, &abort_flag))) break;
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(smem + C::kKOff + s * C::kTileBytes);
+        if (kS >= n_items) return false;
+        if (tS == 0 && !(ok = mbar_wait(&bars.q_full[kS & 1], (kS >> 1) & 1, &abort_flag))) return false;
+        const int st = gS % kStages;
+        if (!(ok = mbar_wait(&bars.kv_full[st], (gS / kStages) & 1, &abort_flag))) return false;
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(smem + C::kQOff + (kS & 1) * C::kTileBytes);
+        const uint32_t k_addr = smem_u32(smem + C::kKOff + st * C::kTileBytes);
 #pragma unroll
-          for (int ks = 0; ks < DH / 16; ++ks) {
-            const uint64_t adesc = sdesc(q_addr + ks * 32, 16, C::kSBO, C::kSwizzle);
-            const uint64_t bdesc = sdesc(k_addr + ks * 32, 16, C::kSBO, C::kSwizzle);
-            mma_ss(tmem + kSCol, adesc, bdesc, idesc_s, ks > 0 ? 1u : 0u);
-          }
-          mma_commit(&bars.s_full);
+        for (int ks = 0; ks < DH / 16; ++ks)
+          mma_ss(tmem + (gS % kSets) * 128, sdesc(q_addr + ks * 32, 16, C::kSBO, C::kSwizzle),
+                 sdesc(k_addr + ks * 32, 16, C::kSBO, C::kSwizzle), idesc_s, ks > 0 ? 1u : 0u);
+        mma_commit(&bars.st_full[gS % kSets]);
+        ++tS;
+        ++gS;
+        return true;
+      };
+      for (int i = 0; i < kSets && ok; ++i)
+        if (!issue_next_s()) break;
+      // PV cursor
+      int kP = 0, g = 0;
+      int nP_next = n_items > 0 ? item_ntiles(item_id(0)) : 0;
+      for (; ok && kP < n_items; ++kP) {
+        const int n = nP_next;
+        nP_next = kP + 1 < n_items ? item_ntiles(item_id(kP + 1)) : 0;
+        const int ob = kP & 1;
+        if (kP >= 2 && !(ok = mbar_wait(&bars.o_free[ob], ((kP - 2) >> 1) & 1, &abort_flag))) break;
+        for (int t = 0; ok && t < n; ++t, ++g) {
+          const int set = g % kSets;
+          if (!(ok = mbar_wait(&bars.p_full[set], (g / kSets) & 1, &abort_flag))) break;
+          tc_fence_after();
+          const uint32_t v_addr = smem_u32(smem + C::kVOff + (g % kStages) * C::kTileBytes);
+#pragma unroll
+          for (int ks = 0; ks < RT_TILE / 16; ++ks)  // O += P_g V_g
+            mma_ts(tmem + kOMain + ob * DH, tmem + set * 128 + ks * 8,
+                   sdesc(v_addr + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_o,
+                   (t > 0 || ks > 0) ? 1u : 0u);
+          mma_commit(&bars.o_done[set]);
+          mma_commit(&bars.kv_empty[g % kStages]);
+          if (t == n - 1) mma_commit(&bars.item_done[ob]);
+          issue_next_s();  // into the S buffer P_g just left
         }
+        if (n == 0) mma_commit(&bars.item_done[ob]);
       }
-      // Drain: all issued MMAs complete before TMEM is released.
       mma_commit(&bars.drain);
       volatile int no_abort = 0;
       mbar_wait(&bars.drain, 0, &no_abort);
     }
-  } else {
-    // ---------------- softmax warpgroup ----------------
+  } else if (warp < 2 + kEpiWarps) {
+    // ---------------- epilogue warpgroup ----------------
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
-    const uint32_t* masks = plan.tile_masks + ((size_t)row_list * T) * RT_TILE * 4;
     const float c = scale_log2;
-    const float kNegInf = -INFINITY;
-    float m_run = kNegInf;  // running row max of raw scores (scale not applied)
-    float2 l2 = make_float2(0.f, 0.f);
-    auto load_mask = [&](int ent) {
-      uint4 mk = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
-      if (ent >= 0) mk = __ldg(reinterpret_cast<const uint4*>(masks + ((size_t)(ent & 0x7FFFFFFF) * RT_TILE + row) * 4));
-      return mk;
+    auto put_sdiag = [&](int k) {
+      const ItemCoord ic = item_coord(item_id(k), H, T);
+      const int qrow = ic.qt * RT_TILE + row;
+      s_sdiag[k & 1][row] =
+          qrow < S ? diag_logit<DH>(qg, kg, ((size_t)(ic.b * H + ic.h)) * S + qrow) : 0.f;
+      mbar_arrive_warp(&bars.sdiag_full[k & 1]);
     };
-    uint4 mk_next = n_tiles > 0 ? load_mask(s_list[0]) : make_uint4(0u, 0u, 0u, 0u);
+    for (int k = 0; k < 2 && k < n_items; ++k) put_sdiag(k);
     bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      const bool full = s_list[j] < 0;
-      const uint4 mk = mk_next;
-      if (j + 1 < n_tiles) mk_next = load_mask(s_list[j + 1]);
-      if (!(ok = mbar_wait(&bars.s_full, j & 1, &abort_flag))) break;
+    for (int k = 0; ok && k < n_items; ++k) {
+      const int item = item_id(k);
+      const ItemCoord ic = item_coord(item, H, T);
+      const int bh = ic.b * H + ic.h;
+      const int qrow = ic.qt * RT_TILE + row;
+      const int n = item_ntiles(item);
+      if (!(ok = mbar_wait_warp(&bars.lsum_full[k & 1], (k >> 1) & 1, &abort_flag))) break;
+      float l = 0.f;
+#pragma unroll
+      for (int s2 = 0; s2 < kSets; ++s2) l += s_lpart[k & 1][s2][row];
+      const float sd = s_sdiag[k & 1][row];
+      if (k + 2 < n_items) put_sdiag(k + 2);  // sets finished item k: both buffers' readers are done
+      if (!(ok = mbar_wait_warp(&bars.item_done[k & 1], (k >> 1) & 1, &abort_flag))) break;
       tc_fence_after();
-      uint32_t r[128];
-      {
-        uint32_t (&r0)[64] = *reinterpret_cast<uint32_t(*)[64]>(&r[0]);
-        uint32_t (&r1)[64] = *reinterpret_cast<uint32_t(*)[64]>(&r[64]);
-        tmem_ld64(lane_base + kSCol, r0);
-        tmem_ld64(lane_base + kSCol + 64, r1);
+      uint32_t o[DH];
+#pragma unroll
+      for (int cc = 0; cc < DH; cc += 32) {
+        uint32_t (&oc)[32] = *reinterpret_cast<uint32_t(*)[32]>(&o[cc]);
+        tmem_ld32(lane_base + kOMain + (k & 1) * DH + cc, oc);
       }
       tmem_wait_ld();
-      if (!full) {
+      tc_fence_before();
+      mbar_arrive_warp(&bars.o_free[k & 1]);
+      // accept the row only well inside the fp32 range (see above); also rejects NaN / inf
+      bool bad = !(l < 0x1p100f);
+      if (n > 0) {  // an item without tiles leaves its O buffer untouched
+#pragma unroll
+        for (int e = 0; e < DH; ++e) bad |= !(fabsf(__uint_as_float(o[e])) < 0x1p120f);
+      }
+      if (qrow < S) {
+        const float inv_l = (n > 0 && l > 0.f) ? 1.f / l : 0.f;
+        if (!bad) {
+          uint4* dst = reinterpret_cast<uint4*>(out + ((size_t)bh * S + qrow) * DH);
+#pragma unroll
+          for (int cc = 0; cc < DH; cc += 8) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 8; e += 2)
+              w[e / 2] = n > 0 ? pack_bf16x2(__uint_as_float(o[cc + e]) * inv_l, __uint_as_float(o[cc + e + 1]) * inv_l)
+                               : 0u;
+            dst[cc / 8] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+        lse[(size_t)bh * S + qrow] =
+            bad ? __int_as_float(0x7FC00000) : (sd * c + kRefShift + __log2f(l)) * 0.6931471805599453f;
+      }
+    }
+    tc_fence_before();
+  } else {
+    // ---------------- softmax sets ----------------
+    const int sw = warp - 2 - kEpiWarps;
+    const int set = sw / kSetWarps;
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+    const uint32_t sbuf = lane_base + (uint32_t)(set * 128);
+    const float c = scale_log2;
+    const float2 c2 = make_float2(c, c);
+    bool ok = true;
+    int g = 0;  // global tile index at the start of the current item
+    int n_next = n_items > 0 ? item_ntiles(item_id(0)) : 0;
+    for (int k = 0; ok && k < n_items; ++k) {
+      const int n = n_next;
+      n_next = k + 1 < n_items ? item_ntiles(item_id(k + 1)) : 0;
+      if (!(ok = mbar_wait_warp(&bars.sdiag_full[k & 1], (k >> 1) & 1, &abort_flag))) break;
+      const float nref = -(s_sdiag[k & 1][row] * c + kRefShift);
+      const float2 nm2 = make_float2(nref, nref);
+      float2 lsum[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      int t = (set - g % kSets + kSets) % kSets;  // first tile of this item owned by this set
+      for (; t < n; t += kSets) {
+        const int gt = g + t;
+        const int u = gt / kSets;  // this set's tile count = phase of its barriers
+        if (!(ok = mbar_wait_warp(&bars.st_full[set], u & 1, &abort_flag))) break;
+        // S_gt issued implies its K / V / mask stage and tile info are in shared memory
+        if (!(ok = mbar_wait_warp(&bars.kv_full[gt % kStages], (gt / kStages) & 1, &abort_flag))) break;
+        tc_fence_after();
+        const uint32_t info = s_info[gt % kInfoRing];
+        const bool full = (info & kInfoFull) != 0;
+        uint4 mk = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
+        if (!full) mk = *reinterpret_cast<const uint4*>(smem + C::kMOff + (gt % kStages) * kMaskBytes + row * 16);
         const uint32_t mw[4] = {mk.x, mk.y, mk.z, mk.w};
 #pragma unroll
-        for (int e = 0; e < 128; ++e)
-          r[e] = ((mw[e >> 5] >> (e & 31)) & 1u) ? r[e] : __float_as_uint(kNegInf);
-      }
-      float mx = kNegInf;
+        for (int ch = 0; ch < 4; ++ch) {  // 32 columns; P of chunk ch lands in columns [16 ch, 16 ch + 16)
+          uint32_t r[32];
+          tmem_ld32(sbuf + ch * 32, r);
+          tmem_wait_ld();
+          if (!full) {
 #pragma unroll
-      for (int e = 0; e < 128; e += 2) mx = fmax3(mx, __uint_as_float(r[e]), __uint_as_float(r[e + 1]));
-      const float m_new = fmaxf(m_run, mx);
-      const bool need = (m_new != kNegInf) && (m_run == kNegInf || (m_new - m_run) * c > kRescaleThreshold);
-      if (j > 0 && !(ok = mbar_wait(&bars.o_done, (j - 1) & 1, &abort_flag))) break;
-      tc_fence_after();
-      if (__any_sync(0xFFFFFFFFu, need)) {
-        const float alpha = m_run == kNegInf ? 0.f : (m_new == kNegInf ? 1.f : fast_exp2((m_run - m_new) * c));
-        if (j > 0) {
-#pragma unroll
-          for (int cc = 0; cc < DH; cc += 32) {
-            uint32_t o[32];
-            tmem_ld32(lane_base + kOCol + cc, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st32(lane_base + kOCol + cc, o);
+            for (int e = 0; e < 32; ++e) r[e] = ((mw[ch] >> e) & 1u) ? r[e] : __float_as_uint(-INFINITY);
           }
-          tmem_wait_st();
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+#pragma unroll
+            for (int a = 0; a < 2; ++a) {
+              const float2 x =
+                  ffma2(make_float2(__uint_as_float(r[e + 2 * a]), __uint_as_float(r[e + 2 * a + 1])), c2, nm2);
+              const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+              lsum[a] = fadd2(lsum[a], p);
+              pk[(e >> 1) + a] = pack_bf16x2(p.x, p.y);
+            }
+          }
+          tmem_st16(sbuf + ch * 16, pk);
         }
-        l2.x *= alpha;
-        l2.y *= alpha;
-        if (m_new != kNegInf) m_run = m_new;
+        tmem_wait_st();
+        // the MMA thread has seen this set's previous P before this one completes
+        if (u > 0 && !(ok = mbar_wait_warp(&bars.o_done[set], (u - 1) & 1, &abort_flag))) break;
+        tc_fence_before();
+        mbar_arrive_warp(&bars.p_full[set]);
       }
-      // p = exp2(c * (s - m)); masked entries hold -inf and give exactly 0
-      const float nmc = m_run == kNegInf ? 0.f : -m_run * c;
-      const float2 cc2 = make_float2(c, c);
-      const float2 nm2 = make_float2(nmc, nmc);
-      uint32_t pk[64];
-#pragma unroll
-      for (int e = 0; e < 128; e += 2) {
-        const float2 x = ffma2(make_float2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), cc2, nm2);
-        const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
-        l2 = fadd2(l2, p);
-        pk[e >> 1] = pack_bf16x2(p.x, p.y);
-      }
-      {
-        uint32_t (&p0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&pk[0]);
-        uint32_t (&p1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&pk[32]);
-        tmem_st32(lane_base + kPCol, p0);
-        tmem_st32(lane_base + kPCol + 32, p1);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&bars.p_full);
-    }
-    const float l_run = l2.x + l2.y;
-    // epilogue
-    if (ok && n_tiles > 0 && mbar_wait(&bars.o_done, (n_tiles - 1) & 1, &abort_flag)) {
-      tc_fence_after();
-      const int q = qt * RT_TILE + row;
-      const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
-      uint16_t* orow = out + ((size_t)bh * S + q) * DH;
-#pragma unroll
-      for (int cc = 0; cc < DH; cc += 16) {
-        uint32_t o[16];
-        tmem_ld16(lane_base + kOCol + cc, o);
-        tmem_wait_ld();
-        uint32_t pko[8];
-#pragma unroll
-        for (int e = 0; e < 16; e += 2)
-          pko[e / 2] = pack_bf16x2(__uint_as_float(o[e]) * inv_l, __uint_as_float(o[e + 1]) * inv_l);
-        if (q < S) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + cc);
-          dst[0] = make_uint4(pko[0], pko[1], pko[2], pko[3]);
-          dst[1] = make_uint4(pko[4], pko[5], pko[6], pko[7]);
-        }
-      }
-      if (q < S)
-        lse[(size_t)bh * S + q] =
-            l_run > 0.f ? (m_run * c + __log2f(l_run)) * 0.6931471805599453f : -INFINITY;
+      g += n;
+      s_lpart[k & 1][set][row] = (lsum[0].x + lsum[0].y) + (lsum[1].x + lsum[1].y);
+      mbar_arrive_warp(&bars.lsum_full[k & 1]);
     }
     tc_fence_before();
   }
@@ -288,31 +538,40 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc(tmem, kMainTmemCols);
   }
 }
 
 template <int DH>
 int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, float scale,
            const rt_tile_plan& plan, uint16_t* o, float* lse, cudaStream_t stream) {
-  using C = Cfg<DH>;
+  using M = MainCfg<DH>;
   CUtensorMap tq, tk, tv;
   if (make_qkv_tensor_map(&tq, q, B * H, S, DH) != RT_OK || make_qkv_tensor_map(&tk, k, B * H, S, DH) != RT_OK ||
       make_qkv_tensor_map(&tv, v, B * H, S, DH) != RT_OK)
     return RT_ERR_CUDA;  // detail recorded by make_qkv_tensor_map
   static bool configured[64] = {false};
+  static int num_sms[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(attn_fwd_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kDynSmem);
+    cudaError_t e =
+        cudaFuncSetAttribute(attn_fwd_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, M::kDynSmem);
     if (e != cudaSuccess) return cuda_failure(e, "cudaFuncSetAttribute(attn_fwd_kernel)");
+    e = cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_failure(e, "cudaDeviceGetAttribute(multiprocessor count)");
     configured[dev] = true;
   }
   const float scale_log2 = scale * 1.4426950408889634f;
-  dim3 grid(plan.tiles, H, B);
-  attn_fwd_kernel<DH><<<grid, kThreads, C::kDynSmem, stream>>>(tq, tk, tv, plan, H, S, scale_log2, o, lse);
-  return check_launch("attn_fwd_kernel launch");
+  const int sms = dev >= 0 && dev < 64 ? num_sms[dev] : 148;
+  const long long items = (long long)B * H * plan.tiles;
+  const int grid = (int)std::min<long long>(items, sms);
+  attn_fwd_kernel<DH><<<grid, kMainThreads, M::kDynSmem, stream>>>(tq, tk, tv, q, k, plan, H, S, scale_log2, o, lse);
+  if (int st = check_launch("attn_fwd_kernel launch")) return st;
+  const long long rows = (long long)B * H * S;
+  const int fix_blocks = (int)std::min<long long>((rows + 255) / 256, 4LL * (dev >= 0 && dev < 64 ? num_sms[dev] : 148));
+  attn_fwd_rowfix_kernel<DH><<<fix_blocks, 256, 0, stream>>>(q, k, v, plan, H, S, scale_log2, o, lse);
+  return check_launch("attn_fwd_rowfix_kernel launch");
 }
 
 }  // namespace fwd

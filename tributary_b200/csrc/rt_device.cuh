@@ -51,6 +51,14 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// One arrival per warp (barrier counts warps): the lanes' prior writes and
+// tcgen05 fences are ordered before lane 0's arrive by the warp sync.
+// Per-thread arrivals would serialise dozens of atomic updates on one word.
+__device__ __forceinline__ void mbar_arrive_warp(uint64_t* bar) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+}
+
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
                "r"(bytes)
@@ -69,22 +77,42 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the warp is parked by the hardware until
+// the phase completes or about `ns` nanoseconds pass, instead of re-polling
+// (re-polling warps crowd the MIO queue that TMEM and shared memory use).
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity to complete. Returns false
 // (and leaves the abort flag set) if the block is aborting or the wait ran out.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 31u) == 0u) {
-      if (*abort_flag) return false;
-      if (clock64() - t0 > RT_WAIT_CYCLES) {
-        *abort_flag = 1;
-        raise_status(RT_ERR_TIMEOUT);
-        return false;
-      }
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > RT_WAIT_CYCLES) {
+      *abort_flag = 1;
+      raise_status(RT_ERR_TIMEOUT);
+      return false;
     }
   }
+}
+
+// mbar_wait for code that the whole warp runs together: every lane gets the
+// same answer, so a timeout cannot split the warp before a .sync.aligned
+// instruction (tcgen05.ld / st, shuffles).
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  return __all_sync(0xFFFFFFFFu, mbar_wait(bar, parity, abort_flag));
 }
 
 // ---------------------------------------------------------------------------
@@ -289,6 +317,18 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    smem_u32(bar))
                : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// register reallocation between warpgroups (all 4 warps of a warpgroup execute it)
+// ---------------------------------------------------------------------------
+template <uint32_t N>
+__device__ __forceinline__ void regs_release() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_claim() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // ---------------------------------------------------------------------------
