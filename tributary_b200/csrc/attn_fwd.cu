@@ -171,7 +171,9 @@ struct MainCfg {
   static constexpr int kVOff = kKOff + kStages * kTileBytes;       // V ring
   static constexpr int kMOff = kVOff + kStages * kTileBytes;       // mask ring
   static constexpr int kSmemBytes = kMOff + kStages * kMaskBytes;
-  static constexpr int kDynSmem = kSmemBytes + 1024;
+  // all 512 TMEM columns per CTA: ask for enough shared memory that a second
+  // CTA never lands on the same SM (it would only wait in tcgen05.alloc)
+  static constexpr int kDynSmem = (kSmemBytes + 1024) > 118 * 1024 ? (kSmemBytes + 1024) : 118 * 1024;
 };
 
 struct __align__(8) MainBarriers {
