@@ -56,20 +56,15 @@ def measured_peaks():
 
 
 def make_metadata(cfg, seed):
-    from oracle import rt_oracle as orc  # workload generator only (seeded synthetic batch)
-    return orc.make_batch(seed, cfg["B"], cfg["S"], cfg["tables"], cfg["cells_lo"], cfg["cells_hi"],
-                          cfg["p_fk"], cfg["pad"], max_parents=cfg["max_parents"])
+    """Seeded synthetic token metadata and the sampler's cell orderings."""
+    from tributary_b200 import batch as rb
+    return rb.make_batch(seed, cfg["B"], cfg["S"], cfg["tables"], cfg["cells_lo"], cfg["cells_hi"],
+                         cfg["p_fk"], cfg["pad"], max_parents=cfg["max_parents"])
 
 
 def perm_for(bt, kind):
-    if kind == 0:
-        return bt["col_perm"]
-    if kind == 1:
-        return bt["out_perm"]
-    if kind == 2:
-        return bt["in_perm"]
-    b, s = bt["seq_row_ids"].shape
-    return np.broadcast_to(np.arange(s, dtype=np.uint16), (b, s)).copy()
+    from tributary_b200 import batch as rb
+    return rb.order_for_kind(bt, kind)
 
 
 # ----------------------------------------------------------------------------

@@ -103,6 +103,26 @@ int rt_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids,
                        int32_t max_rows, int32_t kind, const rt_tile_plan* plan,
                        void* stream);
 
+/* Host-side cell orderings (CPU memory, synchronous; samples run on host
+ * threads). The permutations the sampler attaches to every batch and under
+ * which the kernels run the masks: column -> rt_column_order, feature ->
+ * rt_rcm_order(outbound = 1), neighbor -> rt_rcm_order(outbound = 0).
+ * rt_column_order replaces headwater/src/sampler.rs:655-668: cells sorted by
+ * (padding last, column id, position).
+ *   column_ids [batch][seq_len] int32, is_padding [batch][seq_len] uint8
+ *   perm       [batch][seq_len] uint16 (output), seq_len <= 65536 */
+int rt_column_order(const int32_t* column_ids, const uint8_t* is_padding, int32_t batch,
+                    int32_t seq_len, uint16_t* perm);
+
+/* rt_rcm_order replaces headwater/src/sampler.rs:672-784: a reverse
+ * Cuthill-McKee order of each sample's rows over its FK graph (fk_adj[i][j]
+ * for outbound, fk_adj[j][i] for inbound), then cells sorted by (padding last,
+ * row rank, position). fk_adj [batch][max_rows][max_rows] uint8 (child,
+ * parent), seq_row_ids [batch][seq_len] uint16. Returns RT_ERR_WORKSPACE if
+ * host memory for the sort ran out. */
+int rt_rcm_order(const uint8_t* fk_adj, const uint16_t* seq_row_ids, const uint8_t* is_padding,
+                 int32_t batch, int32_t seq_len, int32_t max_rows, int32_t outbound, uint16_t* perm);
+
 /* Forward: replaces layers.py:83-94 (logits * scale, masked softmax, PV) for
  * inputs already normalised (q_hat * tau, k_hat; layers.py:65-80).
  *   q, k, v [batch][heads][seq_len][head_dim] bf16;  head_dim in {32, 64}

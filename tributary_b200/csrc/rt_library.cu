@@ -7,3 +7,4 @@
 #include "attn_bwd.cu"
 #include "api.cu"
 #include "attn_bwd_noalloc.cu"
+#include "row_order.cu"
