@@ -40,6 +40,11 @@ CONFIGS = {
     # B=32, S=1024, 8 heads x 32; 6 tables, 4-16 cells, p_fk 0.7, 10% padding
     "b": dict(name="rt_attn_fwd_bwd_b32_s1024_h8_d32", B=32, S=1024, H=8, Dh=32,
               tables=6, cells_lo=4, cells_hi=16, p_fk=0.7, max_parents=1, pad=0.10),
+    # full encoder training step, data-parallel: 12 layers, d_model 512, 8 heads x 64,
+    # each layer column -> feature -> neighbor -> full attention + SwiGLU FFN; per-GPU B=32, S=1024
+    "d": dict(name="rt_encoder_train_b32_s1024_l12_d512_h8x64", train=True, B=32, S=1024, H=8, Dh=64,
+              d_model=512, d_ff=1536, layers=12, d_text=384, d_time=8, n_categories=4096,
+              tables=6, cells_lo=4, cells_hi=16, p_fk=0.7, max_parents=1, pad=0.10),
 }
 
 FLOPS_PER_LIVE_TILE = {"fwd": 4, "bwd": 10}  # x 128^2 x Dh per live (b, h, tile pair)
@@ -440,6 +445,232 @@ def run_our_arm(args, cfg):
         dist.destroy_process_group()
 
 
+# ----------------------------------------------------------------------------
+# full encoder training step (config d): data-parallel, NCCL gradient all-reduce
+# ----------------------------------------------------------------------------
+TRAIN_KINDS = (0, 1, 2, 3)
+CELL_ARRAYS = ("seq_row_ids", "column_ids", "is_padding", "fk_adj", "col_perm", "out_perm", "in_perm", "stypes",
+               "numeric_values", "timestamp_values", "bool_values", "categorical_ids", "text_ids", "text_vectors",
+               "is_null", "is_target")
+
+
+def make_train_cells(cfg, seed):
+    from tributary_b200 import batch as rb
+    return rb.make_cells(seed, cfg["B"], cfg["S"], cfg["tables"], cfg["cells_lo"], cfg["cells_hi"], cfg["p_fk"],
+                         cfg["pad"], max_parents=cfg["max_parents"], d_text=cfg["d_text"], d_time=cfg["d_time"],
+                         n_categories=cfg["n_categories"])
+
+
+def encoder_config(cfg, layers=None):
+    from tributary_b200.encoder import EncoderConfig
+    return EncoderConfig(d_model=cfg["d_model"], n_heads=cfg["H"], d_head=cfg["Dh"], d_ff=cfg["d_ff"],
+                         n_layers=layers or cfg["layers"], d_text=cfg["d_text"], d_time=cfg["d_time"],
+                         kinds=TRAIN_KINDS)
+
+
+def cells_to_host_tensors(cells):
+    import torch
+    out = {}
+    for k in CELL_ARRAYS:
+        a = cells[k].astype(np.int32) if cells[k].dtype == np.uint16 else cells[k]
+        out[k] = torch.from_numpy(np.ascontiguousarray(a))
+    return out
+
+
+def train_flops(model, cfg, masks, tokens):
+    """Algorithmic FLOPs of one training step on one rank: 6 x (Linear
+    weights) x tokens for every matmul of the model (forward 2, backward 4),
+    the categorical loss logits, and 14 x 128^2 x Dh per live (b, h, tile pair)
+    of every attention sublayer (forward 4, backward 10)."""
+    import torch.nn as nn
+    lin = sum(m.in_features * m.out_features for m in model.modules() if isinstance(m, nn.Linear))
+    lin_flops = 6 * lin * tokens
+    logits = 6 * tokens * model.cfg.max_categories * cfg["d_model"]
+    attn = 0
+    for _, plan in masks:
+        attn += 14 * 128 * 128 * cfg["Dh"] * cfg["H"] * plan.nnz()
+    return lin_flops + logits + attn * cfg["layers"], attn * cfg["layers"]
+
+
+def run_train_arm(args, cfg):
+    import torch
+    from tributary_b200.attention import device_status
+    from tributary_b200.encoder import RTEncoder
+    from tributary_b200.train import TrainStep, build_masks
+    world, rank, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    cells = make_train_cells(cfg, 1000 + rank)
+    host = {k: v.pin_memory() for k, v in cells_to_host_tensors(cells).items()}
+    d = {k: v.to(dev) for k, v in host.items()}
+    for k in ("target_stype", "cat_start"):
+        d[k] = cells[k]
+    col = torch.from_numpy(cells["col_table"]).to(dev)
+    cat = torch.from_numpy(cells["cat_table"]).to(dev)
+    torch.manual_seed(1234)  # identical initial weights on every rank
+    model = RTEncoder(encoder_config(cfg)).to(dev)
+    step = TrainStep(model)
+
+    def one_step():
+        return step(d, build_masks(d, TRAIN_KINDS), col, cat)
+
+    for _ in range(args.warmup):
+        one_step()
+    barrier(world)
+    if device_status(reset=True) != 0:
+        raise RuntimeError("device status error during warm-up")
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        loss = one_step()
+    e1.record()
+    barrier(world)
+    clocks = sampler.stop()
+    step_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    # end to end: every step copies its cell arrays from pinned host memory and reads the loss back
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    barrier(world)
+    e0.record()
+    for _ in range(args.steps):
+        for k, v in host.items():
+            d[k].copy_(v, non_blocking=True)
+        loss_val = one_step().item()
+    e1.record()
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    status = device_status(reset=True)
+    if status != 0 or not math.isfinite(loss_val):
+        raise RuntimeError(f"device status {status}, loss {loss_val}")
+    tokens = cfg["B"] * cfg["S"]
+    flops, attn_flops = train_flops(model, cfg, build_masks(d, TRAIN_KINDS), tokens)
+    peak_tf, _, peak_src = measured_peaks()
+    achieved = flops / (step_ms * 1e-3) / 1e12
+    n_params = sum(p.numel() for p in model.parameters())
+    if rank == 0:
+        line = {
+            "metric": "rt_encoder_train_tokens_per_s", "value": world * tokens / (step_ms * 1e-3), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": cfg["name"], "B_per_gpu": cfg["B"], "global_batch": world * cfg["B"],
+                       "S": cfg["S"], "layers": cfg["layers"], "d_model": cfg["d_model"], "heads": cfg["H"],
+                       "Dh": cfg["Dh"], "params": n_params, "masks_per_layer": [KIND_NAMES[k] for k in TRAIN_KINDS],
+                       "optimizer": "muon (2-D weights) + adamw, global-norm clip 1.0",
+                       "l2": "working set (activations of 48 sublayers) far above L2",
+                       "parallelism": f"dp{world}: NCCL all-reduce (average) of fp32 gradients in "
+                                      f"{len(step.buckets.buffers)} buckets, overlapped with backward"},
+            "roofline": {"bound": "tensor", "kernel": "whole training step (matmuls + attention)",
+                         "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
+                         "peak_source": peak_src + " bf16 dense (burst)", "traffic": None,
+                         "attention_share_of_flops": attn_flops / flops},
+            "e2e": {"value": world * tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": 4},
+            "gpu_launches": args.steps * (10 + cfg["layers"] * len(TRAIN_KINDS) * 5),
+            "clocks": clocks,
+            "final_loss": loss_val,
+        }
+        if not args.no_cpu_baseline:
+            v, sample = train_cpu_sample(cfg, args.cpu_seconds)
+            line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": len(os.sched_getaffinity(0)),
+                                    "kind": "port", "sample": sample}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+class _CpuOps:
+    """The sublayer's gather, QK normalisation, dense masked attention and
+    scatter in plain torch with the reference's semantics (layers.py:63-97,
+    139-167), for the CPU baseline."""
+
+    @staticmethod
+    def qk_prepare(qkv, order, tau, heads, head_dim):
+        import torch
+        b, s, w = qkv.shape
+        x = torch.gather(qkv, 1, order[:, :, None].expand(b, s, w)).view(b, s, 3, heads, head_dim)
+        x = x.permute(2, 0, 3, 1, 4)
+        q = x[0] / x[0].norm(dim=-1, keepdim=True).clamp_min(1e-6) * tau.view(1, heads, 1, 1)
+        k = x[1] / x[1].norm(dim=-1, keepdim=True).clamp_min(1e-6)
+        return q, k, x[2]
+
+    @staticmethod
+    def attention(q, k, v, mask, scale):
+        import torch
+        s = torch.einsum("bhid,bhjd->bhij", q, k) * scale
+        s = torch.where(mask[:, None], s, torch.full_like(s, -1e9))
+        return torch.einsum("bhij,bhjd->bhid", torch.softmax(s, -1), v)
+
+    @staticmethod
+    def heads_unpermute(o, order):
+        import torch
+        b, h, s, dh = o.shape
+        o = o.permute(0, 2, 1, 3).reshape(b, s, h * dh)
+        inv = torch.empty_like(order).scatter_(1, order, torch.arange(s).expand_as(order))
+        return torch.gather(o, 1, inv[:, :, None].expand(b, s, h * dh))
+
+
+def train_cpu_sample(cfg, budget_s):
+    """The same training step on the host cores: the encoder in fp32 with the
+    reference's dense masked attention (layers.py:83-97) under the oracle's
+    masks, one sample of the batch, for about budget_s seconds."""
+    import torch
+    from oracle import rt_oracle as orc  # CPU baseline leg
+    from tributary_b200.encoder import RTEncoder
+    from tributary_b200.train import TrainStep
+    one = dict(cfg, B=1)
+    cells = make_train_cells(one, 4321)
+    c = cells_to_host_tensors(cells)
+    for k in ("target_stype", "cat_start"):
+        c[k] = cells[k]
+    col = torch.from_numpy(cells["col_table"])
+    cat = torch.from_numpy(cells["cat_table"])
+    masks = []
+    for kind in TRAIN_KINDS:
+        from tributary_b200 import batch as rb
+        perm = rb.order_for_kind(cells, kind)
+        m = orc.permute_mask(orc.mask_for_kind(kind, cells["seq_row_ids"], cells["fk_adj"], cells["column_ids"],
+                                               cells["is_padding"]), perm)
+        masks.append((torch.from_numpy(perm.astype(np.int64)), torch.from_numpy(m)))
+    torch.manual_seed(1234)
+    model = RTEncoder(encoder_config(one), ops=_CpuOps())
+    step = TrainStep(model, autocast=False)
+    t0 = time.perf_counter()
+    n = 0
+    while n == 0 or time.perf_counter() - t0 < budget_s:
+        step(c, masks, col, cat)
+        n += 1
+    dt = time.perf_counter() - t0
+    return n * cfg["S"] / dt, (f"{n} fp32 training steps of the full {cfg['layers']}-layer encoder on 1 sample "
+                               f"(S={cfg['S']}), dense masked attention, torch CPU, {torch.get_num_threads()} threads")
+
+
+def run_train_reference_arm(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    values, sample = [], ""
+    per_step = max(5.0, min(30.0, 150.0 / max(1, args.steps)))
+    train_cpu_sample(cfg, 1.0)
+    for _ in range(args.steps):
+        v, sample = train_cpu_sample(cfg, per_step)
+        values.append(v)
+    value = statistics.median(values)
+    line = {
+        "impl": "reference", "metric": "rt_encoder_train_tokens_per_s", "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * cfg["B"] * cfg["S"] / value, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": cfg["name"], "B_per_gpu": cfg["B"], "S": cfg["S"], "layers": cfg["layers"]},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": len(os.sched_getaffinity(0)), "kind": "port",
+                         "sample": sample + " (jax/XLA-CPU not installable)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -458,7 +689,9 @@ def main():
     if args.batch is not None:
         cfg["B"] = args.batch
         cfg["name"] = cfg["name"].replace("_b%d_" % CONFIGS[args.config]["B"], "_b%d_" % args.batch)
-    if args.impl == "reference":
+    if cfg.get("train"):
+        (run_train_reference_arm if args.impl == "reference" else run_train_arm)(args, cfg)
+    elif args.impl == "reference":
         run_reference_arm(args, cfg)
     else:
         run_our_arm(args, cfg)

@@ -123,6 +123,37 @@ int rt_column_order(const int32_t* column_ids, const uint8_t* is_padding, int32_
 int rt_rcm_order(const uint8_t* fk_adj, const uint16_t* seq_row_ids, const uint8_t* is_padding,
                  int32_t batch, int32_t seq_len, int32_t max_rows, int32_t outbound, uint16_t* perm);
 
+/* Token preparation of one attention sublayer (device memory, stream-ordered).
+ * rt_qk_prepare replaces the gather of layers.py:139-142 and the QK
+ * normalisation of layers.py:63-80, applied after the QKV projection (a
+ * per-token linear map commutes with the gather):
+ *   qkv   [batch][seq_len][3][heads][head_dim] bf16, token order
+ *   perm  [batch][seq_len] uint16, the sublayer's cell order
+ *   tau   [heads] fp32
+ *   q, k, v [batch][heads][seq_len][head_dim] bf16 in perm order:
+ *     q = tau_h q_raw / max(|q_raw|, 1e-6), k = k_raw / max(|k_raw|, 1e-6), v = v_raw
+ *   rnorm [2][batch][heads][seq_len] fp32: 1 / max(|q_raw|, 1e-6), same for k
+ * head_dim in {32, 64}. */
+int rt_qk_prepare(const uint16_t* qkv, const uint16_t* perm, const float* tau, int32_t batch,
+                  int32_t heads, int32_t seq_len, int32_t head_dim, uint16_t* q, uint16_t* k,
+                  uint16_t* v, float* rnorm, void* stream);
+
+/* Backward of rt_qk_prepare: dqkv in token order from dq, dk, dv in perm
+ * order, and dtau_rows [batch][heads][seq_len] fp32, each row's share of the
+ * gradient of tau_h (d tau_h = the sum of dtau_rows over batch and rows). */
+int rt_qk_prepare_bwd(const uint16_t* dq, const uint16_t* dk, const uint16_t* dv,
+                      const uint16_t* qkv, const uint16_t* perm, const float* tau,
+                      const float* rnorm, int32_t batch, int32_t heads, int32_t seq_len,
+                      int32_t head_dim, uint16_t* dqkv, float* dtau_rows, void* stream);
+
+/* Attention output back to token order (the scatter of layers.py:159-167 and
+ * the head merge of layers.py:99): out[b][perm[b][i]][h*head_dim + d] =
+ * o[b][h][i][d]. rt_heads_permute is the reverse map (its backward). */
+int rt_heads_unpermute(const uint16_t* o, const uint16_t* perm, int32_t batch, int32_t heads,
+                       int32_t seq_len, int32_t head_dim, uint16_t* out, void* stream);
+int rt_heads_permute(const uint16_t* x, const uint16_t* perm, int32_t batch, int32_t heads,
+                     int32_t seq_len, int32_t head_dim, uint16_t* out, void* stream);
+
 /* Forward: replaces layers.py:83-94 (logits * scale, masked softmax, PV) for
  * inputs already normalised (q_hat * tau, k_hat; layers.py:65-80).
  *   q, k, v [batch][heads][seq_len][head_dim] bf16;  head_dim in {32, 64}

@@ -31,6 +31,7 @@ EXPORTED = (
     "rt_tile_plan_bytes", "rt_tile_plan_bind", "rt_build_tile_plan",
     "rt_attention_fwd", "rt_attention_bwd_workspace_bytes", "rt_attention_bwd",
     "rt_attention_bwd_noalloc", "rt_column_order", "rt_rcm_order",
+    "rt_qk_prepare", "rt_qk_prepare_bwd", "rt_heads_unpermute", "rt_heads_permute",
     "rt_device_status", "rt_status_string", "rt_last_error", "rt_version",
 )
 
@@ -73,6 +74,14 @@ def _declare(lib):
     lib.rt_tile_plan_bind.restype = ctypes.c_int
     lib.rt_build_tile_plan.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, i32, plan_p, vp]
     lib.rt_build_tile_plan.restype = ctypes.c_int
+    lib.rt_qk_prepare.argtypes = [vp, vp, vp, i32, i32, i32, i32, vp, vp, vp, vp, vp]
+    lib.rt_qk_prepare.restype = ctypes.c_int
+    lib.rt_qk_prepare_bwd.argtypes = [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp, vp, vp]
+    lib.rt_qk_prepare_bwd.restype = ctypes.c_int
+    lib.rt_heads_unpermute.argtypes = [vp, vp, i32, i32, i32, i32, vp, vp]
+    lib.rt_heads_unpermute.restype = ctypes.c_int
+    lib.rt_heads_permute.argtypes = [vp, vp, i32, i32, i32, i32, vp, vp]
+    lib.rt_heads_permute.restype = ctypes.c_int
     lib.rt_column_order.argtypes = [vp, vp, i32, i32, vp]
     lib.rt_column_order.restype = ctypes.c_int
     lib.rt_rcm_order.argtypes = [vp, vp, vp, i32, i32, i32, i32, vp]

@@ -119,3 +119,58 @@ def order_for_kind(batch: dict, kind: int) -> np.ndarray:
     b, s = batch["seq_row_ids"].shape
     return {MASK_COLUMN: batch["col_perm"], MASK_FEATURE: batch["out_perm"],
             MASK_NEIGHBOR: batch["in_perm"], MASK_FULL: identity_order(b, s)}[kind]
+
+
+STYPE_IDENTIFIER, STYPE_NUMERICAL, STYPE_TIMESTAMP, STYPE_BOOLEAN, STYPE_CATEGORICAL, STYPE_TEXT, STYPE_IGNORED = range(7)
+
+
+def make_cells(seed: int, B: int, S: int, n_tables: int, cells_lo: int, cells_hi: int, p_fk: float,
+               pad_frac: float, max_parents: int = 1, d_text: int = 384, d_time: int = 8,
+               n_categories: int = 4096, max_categories: int = 256, null_frac: float = 0.05,
+               target_frac: float = 0.5, target_stype: int = STYPE_CATEGORICAL) -> dict:
+    """A full training batch: the token metadata of make_batch plus seeded cell
+    values by semantic type, in the layout the encoder consumes (the sampler
+    fields of headwater/src/python.rs:17-91, with values drawn synthetically):
+      stypes [B,S] int8 -- one semantic type per global column (padding:
+        ignored); numeric_values [B,S] f32 ~ N(0,1) (z-scored);
+      timestamp_values [B,S,d_time] f32 -- d_time-1 cyclic features sin/cos of
+        uniform phases, then a z-scored scalar;
+      bool_values [B,S] u8; categorical_ids [B,S] i32 into an n_categories row
+        table, drawn from the first max_categories ids for the target column
+        type; text_ids [B,S] i32 into text_vectors [U, d_text] ~ N(0,1)/sqrt(d_text);
+      is_null [B,S] u8 (null_frac of real cells); is_target [B,S] u8 (target_frac
+        of the cells of the target semantic type); target_stype; cat_start;
+      col_table [C, d_text] and cat_table [n_categories, d_text] ~ N(0,1):
+        the frozen column-name and category embeddings."""
+    meta = make_batch(seed, B, S, n_tables, cells_lo, cells_hi, p_fk, pad_frac, max_parents=max_parents)
+    rng = np.random.Generator(np.random.PCG64(seed + 0x5EED))
+    real = meta["is_padding"] == 0
+    n_cols = int(meta["column_ids"].max()) + 1
+    col_stype = rng.choice(np.array([STYPE_NUMERICAL, STYPE_TIMESTAMP, STYPE_BOOLEAN, STYPE_CATEGORICAL,
+                                     STYPE_TEXT, STYPE_IDENTIFIER], dtype=np.int8),
+                           size=n_cols, p=[0.3, 0.15, 0.1, 0.3, 0.1, 0.05])
+    col_stype[0] = target_stype  # at least one column of the target type
+    stypes = np.where(real, col_stype[meta["column_ids"]], STYPE_IGNORED).astype(np.int8)
+    phases = rng.uniform(0, 2 * np.pi, size=(B, S, (d_time - 1 + 1) // 2)).astype(np.float32)
+    cyc = np.concatenate([np.sin(phases), np.cos(phases)], axis=-1)[..., :d_time - 1]
+    ts = np.concatenate([cyc, rng.standard_normal((B, S, 1), dtype=np.float32)], axis=-1)
+    n_text = max(1, B * S // 4)
+    cat_ids = np.where(stypes == target_stype, rng.integers(0, max_categories, (B, S)),
+                       rng.integers(0, n_categories, (B, S))).astype(np.int32)
+    cells = dict(meta)
+    cells.update(
+        stypes=stypes,
+        numeric_values=rng.standard_normal((B, S), dtype=np.float32),
+        timestamp_values=np.ascontiguousarray(ts, dtype=np.float32),
+        bool_values=rng.integers(0, 2, (B, S)).astype(np.uint8),
+        categorical_ids=cat_ids,
+        text_ids=rng.integers(0, n_text, (B, S)).astype(np.int32),
+        text_vectors=(rng.standard_normal((n_text, d_text), dtype=np.float32) / np.sqrt(d_text)).astype(np.float32),
+        is_null=((rng.random((B, S)) < null_frac) & real).astype(np.uint8),
+        is_target=((rng.random((B, S)) < target_frac) & (stypes == target_stype)).astype(np.uint8),
+        target_stype=int(target_stype),
+        cat_start=0,
+        col_table=rng.standard_normal((n_cols, d_text), dtype=np.float32),
+        cat_table=rng.standard_normal((n_categories, d_text), dtype=np.float32),
+    )
+    return cells

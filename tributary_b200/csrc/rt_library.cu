@@ -6,5 +6,6 @@
 #include "attn_fwd.cu"
 #include "attn_bwd.cu"
 #include "api.cu"
+#include "token_prep.cu"
 #include "attn_bwd_noalloc.cu"
 #include "row_order.cu"

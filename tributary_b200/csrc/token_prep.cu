@@ -1,0 +1,252 @@
+// Token preparation around the attention kernels of one sublayer: the
+// permuted-order gather / scatter of confluence/confluence/layers.py:139-167
+// and the QK L2 normalisation with learned temperature of layers.py:63-80,
+// fused into single memory-bound passes.
+//
+// A per-token linear map commutes with a permutation of the tokens, so the
+// QKV projection runs on the tokens in their own order and the gather moves
+// into these kernels:
+//   qk_prepare   qkv[b, perm[b,i], {q,k,v}, h, :]  ->  q_hat[b,h,i,:] =
+//                tau_h q / max(|q|, 1e-6), k_hat = k / max(|k|, 1e-6), v
+//                (bf16, the attention kernels' [B,H,S,Dh] layout), with the
+//                fp32 inverse norms kept for the backward
+//   qk_prepare_bwd  the normalisation's Jacobian, scattered back through the
+//                permutation (a permutation has no collisions: no atomics)
+//   heads_unpermute / heads_permute  attention output [B,H,S,Dh] in permuted
+//                order <-> [B,S,H*Dh] in token order (each other's backward)
+// One warp per token; a warp moves each head's Dh-element row as one
+// contiguous, coalesced access. Norms and products are accumulated in fp32.
+#include "rt_device.cuh"
+#include "rt_internal.h"
+
+namespace rt {
+namespace tok {
+
+constexpr int kWarps = 8;  // tokens per 256-thread block
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) x += __shfl_xor_sync(0xFFFFFFFFu, x, off);
+  return x;
+}
+
+// Dh / 32 consecutive bf16 per lane: 2 for Dh = 64 (one 32-bit word), 1 for Dh = 32.
+template <int DH>
+struct Lane {
+  static constexpr int kE = DH / 32;
+  float v[kE];
+  __device__ __forceinline__ void load(const uint16_t* row, int lane) {
+    if (kE == 2) {
+      const float2 f = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(row + 2 * lane));
+      v[0] = f.x;
+      v[kE - 1] = f.y;
+    } else {
+      v[0] = __uint_as_float((uint32_t)row[lane] << 16);
+    }
+  }
+  __device__ __forceinline__ void store(uint16_t* row, int lane, float s) const {
+    if (kE == 2) {
+      *reinterpret_cast<uint32_t*>(row + 2 * lane) = pack_bf16x2(v[0] * s, v[kE - 1] * s);
+    } else {
+      const __nv_bfloat16 b = __float2bfloat16_rn(v[0] * s);
+      row[lane] = *reinterpret_cast<const uint16_t*>(&b);
+    }
+  }
+  __device__ __forceinline__ float dot(const Lane& o) const {
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < kE; ++e) s = fmaf(v[e], o.v[e], s);
+    return s;
+  }
+};
+
+template <int DH>
+__device__ __forceinline__ void copy_row(uint16_t* dst, const uint16_t* src, int lane) {
+  if (DH == 64)
+    reinterpret_cast<uint32_t*>(dst)[lane] = reinterpret_cast<const uint32_t*>(src)[lane];
+  else
+    dst[lane] = src[lane];
+}
+
+template <int DH>
+__global__ void __launch_bounds__(32 * kWarps) qk_prepare_kernel(const uint16_t* __restrict__ qkv,
+                                                                 const uint16_t* __restrict__ perm,
+                                                                 const float* __restrict__ tau, int B, int H, int S,
+                                                                 uint16_t* __restrict__ q, uint16_t* __restrict__ k,
+                                                                 uint16_t* __restrict__ v, float* __restrict__ rnorm) {
+  const int lane = threadIdx.x & 31;
+  const long long t = (long long)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (t >= (long long)B * S) return;
+  const int b = (int)(t / S), i = (int)(t % S);
+  const int D = H * DH;
+  const uint16_t* row = qkv + ((size_t)b * S + perm[t]) * 3 * D;
+  for (int h = 0; h < H; ++h) {
+    const size_t o = (((size_t)b * H + h) * S + i) * DH;
+    Lane<DH> x;
+    x.load(row + h * DH, lane);
+    const float rq = 1.f / fmaxf(sqrtf(warp_sum(x.dot(x))), 1e-6f);
+    x.store(q + o, lane, rq * tau[h]);
+    x.load(row + D + h * DH, lane);
+    const float rk = 1.f / fmaxf(sqrtf(warp_sum(x.dot(x))), 1e-6f);
+    x.store(k + o, lane, rk);
+    copy_row<DH>(v + o, row + 2 * D + h * DH, lane);
+    if (lane == 0) {
+      rnorm[((size_t)b * H + h) * S + i] = rq;
+      rnorm[(((size_t)B + b) * H + h) * S + i] = rk;
+    }
+  }
+}
+
+// out = scale * y, y = x r, r = 1 / max(|x|, eps), upstream gradient g:
+// dx = r (dy - y (y . dy)) with dy = scale * g while |x| > eps (r < 1 / eps),
+// else dx = r dy (the clamped norm is a constant). Returns y . g, the row's
+// share of d scale.
+template <int DH>
+__device__ __forceinline__ float norm_bwd(const uint16_t* x_row, const uint16_t* g_row, float r, float scale,
+                                          uint16_t* dx_row, int lane) {
+  Lane<DH> x, g;
+  x.load(x_row, lane);
+  g.load(g_row, lane);
+#pragma unroll
+  for (int e = 0; e < Lane<DH>::kE; ++e) x.v[e] *= r;  // y
+  const float yg = warp_sum(x.dot(g));
+  const float yd = r < 1e6f ? scale * yg : 0.f;
+#pragma unroll
+  for (int e = 0; e < Lane<DH>::kE; ++e) g.v[e] = scale * g.v[e] - x.v[e] * yd;
+  g.store(dx_row, lane, r);
+  return yg;
+}
+
+template <int DH>
+__global__ void __launch_bounds__(32 * kWarps) qk_prepare_bwd_kernel(
+    const uint16_t* __restrict__ dq, const uint16_t* __restrict__ dk, const uint16_t* __restrict__ dv,
+    const uint16_t* __restrict__ qkv, const uint16_t* __restrict__ perm, const float* __restrict__ tau,
+    const float* __restrict__ rnorm, int B, int H, int S, uint16_t* __restrict__ dqkv,
+    float* __restrict__ dtau_rows) {
+  const int lane = threadIdx.x & 31;
+  const long long t = (long long)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (t >= (long long)B * S) return;
+  const int b = (int)(t / S), i = (int)(t % S);
+  const int D = H * DH;
+  const size_t r0 = ((size_t)b * S + perm[t]) * 3 * D;
+  for (int h = 0; h < H; ++h) {
+    const size_t o = (((size_t)b * H + h) * S + i) * DH;
+    const float rq = rnorm[((size_t)b * H + h) * S + i];
+    const float rk = rnorm[(((size_t)B + b) * H + h) * S + i];
+    const float yg = norm_bwd<DH>(qkv + r0 + h * DH, dq + o, rq, tau[h], dqkv + r0 + h * DH, lane);
+    if (lane == 0) dtau_rows[((size_t)b * H + h) * S + i] = yg;
+    norm_bwd<DH>(qkv + r0 + D + h * DH, dk + o, rk, 1.f, dqkv + r0 + D + h * DH, lane);
+    copy_row<DH>(dqkv + r0 + 2 * D + h * DH, dv + o, lane);
+  }
+}
+
+// kToTokens: [B,H,S,Dh] permuted -> [B,S,H*Dh] token order; else the reverse.
+template <int DH, bool kToTokens>
+__global__ void __launch_bounds__(32 * kWarps) heads_reorder_kernel(const uint16_t* __restrict__ src,
+                                                                    const uint16_t* __restrict__ perm, int B, int H,
+                                                                    int S, uint16_t* __restrict__ dst) {
+  const int lane = threadIdx.x & 31;
+  const long long t = (long long)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (t >= (long long)B * S) return;
+  const int b = (int)(t / S), i = (int)(t % S);
+  const size_t tok = ((size_t)b * S + perm[t]) * H * DH;
+  for (int h = 0; h < H; ++h) {
+    const size_t o = (((size_t)b * H + h) * S + i) * DH;
+    if (kToTokens)
+      copy_row<DH>(dst + tok + h * DH, src + o, lane);
+    else
+      copy_row<DH>(dst + o, src + tok + h * DH, lane);
+  }
+}
+
+inline unsigned blocks_for(long long tokens) { return (unsigned)((tokens + kWarps - 1) / kWarps); }
+
+}  // namespace tok
+}  // namespace rt
+
+namespace {
+
+int check_shape(int32_t batch, int32_t heads, int32_t seq_len, int32_t head_dim) {
+  if (batch < 0 || heads < 0 || seq_len < 0 || seq_len > 65536 || heads > 256) return RT_ERR_INVALID_ARGUMENT;
+  if (head_dim != 32 && head_dim != 64) return RT_ERR_UNSUPPORTED;
+  return RT_OK;
+}
+
+bool all_aligned(std::initializer_list<const void*> ps) {
+  for (const void* p : ps)
+    if (!p || !rt::aligned16(p)) return false;
+  return true;
+}
+
+}  // namespace
+
+extern "C" int rt_qk_prepare(const uint16_t* qkv, const uint16_t* perm, const float* tau, int32_t batch,
+                             int32_t heads, int32_t seq_len, int32_t head_dim, uint16_t* q, uint16_t* k,
+                             uint16_t* v, float* rnorm, void* stream) {
+  using namespace rt;
+  if (int st = check_shape(batch, heads, seq_len, head_dim)) return st;
+  if ((long long)batch * heads * seq_len == 0) return RT_OK;
+  if (!all_aligned({qkv, perm, tau, q, k, v, rnorm})) return RT_ERR_INVALID_ARGUMENT;
+  DeviceGuard guard(qkv);
+  if (guard.status() != RT_OK) return guard.status();
+  const unsigned grid = tok::blocks_for((long long)batch * seq_len);
+  auto s = static_cast<cudaStream_t>(stream);
+  if (head_dim == 64)
+    tok::qk_prepare_kernel<64><<<grid, 32 * tok::kWarps, 0, s>>>(qkv, perm, tau, batch, heads, seq_len, q, k, v,
+                                                                 rnorm);
+  else
+    tok::qk_prepare_kernel<32><<<grid, 32 * tok::kWarps, 0, s>>>(qkv, perm, tau, batch, heads, seq_len, q, k, v,
+                                                                 rnorm);
+  return check_launch("qk_prepare_kernel launch");
+}
+
+extern "C" int rt_qk_prepare_bwd(const uint16_t* dq, const uint16_t* dk, const uint16_t* dv, const uint16_t* qkv,
+                                 const uint16_t* perm, const float* tau, const float* rnorm, int32_t batch,
+                                 int32_t heads, int32_t seq_len, int32_t head_dim, uint16_t* dqkv,
+                                 float* dtau_rows, void* stream) {
+  using namespace rt;
+  if (int st = check_shape(batch, heads, seq_len, head_dim)) return st;
+  if ((long long)batch * heads * seq_len == 0) return RT_OK;
+  if (!all_aligned({dq, dk, dv, qkv, perm, tau, rnorm, dqkv, dtau_rows})) return RT_ERR_INVALID_ARGUMENT;
+  DeviceGuard guard(qkv);
+  if (guard.status() != RT_OK) return guard.status();
+  const unsigned grid = tok::blocks_for((long long)batch * seq_len);
+  auto s = static_cast<cudaStream_t>(stream);
+  if (head_dim == 64)
+    tok::qk_prepare_bwd_kernel<64><<<grid, 32 * tok::kWarps, 0, s>>>(dq, dk, dv, qkv, perm, tau, rnorm, batch,
+                                                                     heads, seq_len, dqkv, dtau_rows);
+  else
+    tok::qk_prepare_bwd_kernel<32><<<grid, 32 * tok::kWarps, 0, s>>>(dq, dk, dv, qkv, perm, tau, rnorm, batch,
+                                                                     heads, seq_len, dqkv, dtau_rows);
+  return check_launch("qk_prepare_bwd_kernel launch");
+}
+
+namespace {
+template <bool kToTokens>
+int heads_reorder(const uint16_t* src, const uint16_t* perm, int32_t batch, int32_t heads, int32_t seq_len,
+                  int32_t head_dim, uint16_t* dst, void* stream) {
+  using namespace rt;
+  if (int st = check_shape(batch, heads, seq_len, head_dim)) return st;
+  if ((long long)batch * heads * seq_len == 0) return RT_OK;
+  if (!all_aligned({src, perm, dst})) return RT_ERR_INVALID_ARGUMENT;
+  DeviceGuard guard(src);
+  if (guard.status() != RT_OK) return guard.status();
+  const unsigned grid = tok::blocks_for((long long)batch * seq_len);
+  auto s = static_cast<cudaStream_t>(stream);
+  if (head_dim == 64)
+    tok::heads_reorder_kernel<64, kToTokens><<<grid, 32 * tok::kWarps, 0, s>>>(src, perm, batch, heads, seq_len, dst);
+  else
+    tok::heads_reorder_kernel<32, kToTokens><<<grid, 32 * tok::kWarps, 0, s>>>(src, perm, batch, heads, seq_len, dst);
+  return check_launch("heads_reorder_kernel launch");
+}
+}  // namespace
+
+extern "C" int rt_heads_unpermute(const uint16_t* o, const uint16_t* perm, int32_t batch, int32_t heads,
+                                  int32_t seq_len, int32_t head_dim, uint16_t* out, void* stream) {
+  return heads_reorder<true>(o, perm, batch, heads, seq_len, head_dim, out, stream);
+}
+
+extern "C" int rt_heads_permute(const uint16_t* x, const uint16_t* perm, int32_t batch, int32_t heads,
+                                int32_t seq_len, int32_t head_dim, uint16_t* out, void* stream) {
+  return heads_reorder<false>(x, perm, batch, heads, seq_len, head_dim, out, stream);
+}

@@ -1,0 +1,212 @@
+"""Data-parallel training step of the RT encoder.
+
+One process per GPU; every rank holds a full model replica and its own shard
+of the batch (attention never crosses samples, confluence/confluence/model.py:
+201-264), so the only exchange is the gradient mean over ranks
+(confluence/confluence/train.py:212-214, jax.lax.pmean).
+
+GradBuckets lays the gradients out in flat fp32 buckets (parameters in
+reverse registration order, roughly the order backward produces them) and
+points every parameter's .grad at its slice, so autograd accumulates straight
+into the buckets. A post-accumulate hook counts each bucket's parameters; the
+moment a bucket is complete its all-reduce is launched asynchronously (NCCL
+over NVLink / NVSwitch on GPUs, gloo on CPU) and overlaps the rest of the
+backward pass. finish() waits for all of them.
+
+The optimizer follows confluence/confluence/optimizer.py (optax.contrib.muon):
+Muon -- momentum, Nesterov, then the quintic Newton-Schulz orthogonalisation of
+Jordan et al. (2024) -- for 2-D weights and AdamW for everything else, after
+clipping the global gradient norm (config.py:64).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+
+
+class GradBuckets:
+    def __init__(self, params, group=None, bucket_bytes: int = 32 << 20):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        self.avg = self.world > 1 and dist.get_backend(group) == "nccl"  # NCCL averages in the reduction
+        params = [p for p in params if p.requires_grad]
+        groups, cur, size = [], [], 0
+        for p in reversed(params):
+            if cur and size + 4 * p.numel() > bucket_bytes:
+                groups.append(cur)
+                cur, size = [], 0
+            cur.append(p)
+            size += 4 * p.numel()
+        if cur:
+            groups.append(cur)
+        self.params = groups
+        self.buffers, self.views = [], []
+        for i, grp in enumerate(groups):
+            buf = torch.zeros(sum(p.numel() for p in grp), dtype=torch.float32, device=grp[0].device)
+            off = 0
+            views = []
+            for p in grp:
+                v = buf[off:off + p.numel()].view_as(p)
+                off += p.numel()
+                p.grad = v
+                views.append(v)
+                p.register_post_accumulate_grad_hook(self._hook(i, len(views) - 1))
+            self.buffers.append(buf)
+            self.views.append(views)
+        self.pending = [len(g) for g in groups]
+        self.works = []
+        self.launched = [False] * len(groups)
+
+    @property
+    def bucket_sizes(self):
+        return [b.numel() * 4 for b in self.buffers]
+
+    def _hook(self, i, j):
+        def hook(p):
+            v = self.views[i][j]
+            if p.grad is not v:  # autograd replaced the buffer view: fold it back in
+                if p.grad.data_ptr() != v.data_ptr():
+                    v.copy_(p.grad)
+                p.grad = v
+            self.pending[i] -= 1
+            if self.pending[i] == 0:
+                self._launch(i)
+        return hook
+
+    def _launch(self, i):
+        if self.launched[i]:
+            return
+        self.launched[i] = True
+        if self.world > 1:
+            op = dist.ReduceOp.AVG if self.avg else dist.ReduceOp.SUM
+            self.works.append(dist.all_reduce(self.buffers[i], op=op, group=self.group, async_op=True))
+
+    def zero(self):
+        """Clear the buckets before a backward pass."""
+        for buf in self.buffers:
+            buf.zero_()
+        for grp, views in zip(self.params, self.views):
+            for p, v in zip(grp, views):
+                p.grad = v
+        self.pending = [len(g) for g in self.params]
+        self.launched = [False] * len(self.params)
+        self.works = []
+
+    def finish(self):
+        """Reduce the buckets no hook completed (parameters without a
+        gradient this step), wait for every all-reduce, and turn sums into
+        means where the backend cannot average."""
+        for i in range(len(self.buffers)):
+            self._launch(i)
+        for w in self.works:
+            w.wait()
+        self.works = []
+        if self.world > 1 and not self.avg:
+            for buf in self.buffers:
+                buf.div_(self.world)
+
+    def global_norm(self) -> torch.Tensor:
+        return torch.linalg.vector_norm(torch.stack([torch.linalg.vector_norm(b) for b in self.buffers]))
+
+
+def newton_schulz(g: torch.Tensor, steps: int = 5, eps: float = 1e-7) -> torch.Tensor:
+    """Approximate U V^T of each matrix of a [n, rows, cols] stack by the
+    quintic iteration X <- a X + (b A + c A^2) X, A = X X^T, with
+    (a, b, c) = (3.4445, -4.7750, 2.0315), in bf16 (Jordan et al., 2024)."""
+    a, b, c = 3.4445, -4.7750, 2.0315
+    x = g.to(torch.bfloat16)
+    tall = x.shape[-2] > x.shape[-1]
+    if tall:
+        x = x.transpose(-2, -1)
+    x = x / (torch.linalg.vector_norm(x.float(), dim=(-2, -1), keepdim=True) + eps).to(x.dtype)
+    for _ in range(steps):
+        m = x @ x.transpose(-2, -1)
+        x = a * x + (b * m + c * (m @ m)) @ x
+    if tall:
+        x = x.transpose(-2, -1)
+    return x
+
+
+class Muon:
+    """Momentum + Nesterov + Newton-Schulz orthogonalised updates for 2-D
+    weights, scaled by sqrt(max(1, rows / cols)); matrices of one shape are
+    orthogonalised together as a batch."""
+
+    def __init__(self, params, lr: float = 0.02, beta: float = 0.95, ns_steps: int = 5):
+        self.params = [p for p in params if p.requires_grad]
+        self.lr, self.beta, self.ns_steps = lr, beta, ns_steps
+        self.momentum = [torch.zeros_like(p) for p in self.params]
+        self.by_shape = {}
+        for i, p in enumerate(self.params):
+            self.by_shape.setdefault(tuple(p.shape), []).append(i)
+
+    @torch.no_grad()
+    def step(self):
+        for shape, idx in self.by_shape.items():
+            ms = [self.momentum[i] for i in idx]
+            gs = [self.params[i].grad for i in idx]
+            torch._foreach_mul_(ms, self.beta)
+            torch._foreach_add_(ms, gs)
+            upd = torch.stack(torch._foreach_add(gs, ms, alpha=self.beta))  # Nesterov
+            o = newton_schulz(upd, self.ns_steps)
+            scale = -self.lr * math.sqrt(max(1.0, shape[0] / shape[1]))
+            for k, i in enumerate(idx):
+                self.params[i].add_(o[k].to(self.params[i].dtype), alpha=scale)
+
+
+class TrainStep:
+    """Forward, loss, backward with overlapped gradient all-reduce, clipping
+    and the Muon / AdamW update, for one rank's shard of the batch."""
+
+    def __init__(self, model, group=None, muon_lr: float = 0.02, adamw_lr: float = 3e-4,
+                 weight_decay: float = 0.1, max_grad_norm: float = 1.0, bucket_bytes: int = 32 << 20,
+                 autocast: bool = True):
+        self.model = model
+        self.buckets = GradBuckets(model.parameters(), group, bucket_bytes)
+        mats = [p for p in model.parameters() if p.requires_grad and p.ndim == 2]
+        rest = [p for p in model.parameters() if p.requires_grad and p.ndim != 2]
+        dev = next(model.parameters()).device
+        self.muon = Muon(mats, lr=muon_lr)
+        self.adamw = torch.optim.AdamW(rest, lr=adamw_lr, betas=(0.9, 0.95), eps=1e-8,
+                                       weight_decay=weight_decay, fused=dev.type == "cuda")
+        self.max_grad_norm = max_grad_norm
+        self.autocast = autocast and dev.type == "cuda"
+
+    def __call__(self, cells, masks, col_table, cat_table) -> torch.Tensor:
+        self.buckets.zero()
+        with torch.autocast("cuda", dtype=torch.bfloat16, enabled=self.autocast):
+            out = self.model(cells, masks, col_table, cat_table)
+            loss = self.model.loss(out, cells, cat_table)
+        loss.backward()
+        self.buckets.finish()
+        norm = self.buckets.global_norm()
+        clip = torch.clamp(self.max_grad_norm / (norm + 1e-6), max=1.0)
+        torch._foreach_mul_(self.buckets.buffers, clip)
+        self.muon.step()
+        self.adamw.step()
+        return loss.detach()
+
+
+def build_masks(meta: dict, kinds, max_rows: int | None = None):
+    """Per sublayer kind: (int16 cell order, tile plan), on the device of
+    ``meta`` (batch.make_cells arrays moved to the GPU). The plans are rebuilt
+    for every batch, as build_attention_masks is inside the reference's jitted
+    step (model.py:299-313)."""
+    from . import attention as rt
+    from .batch import MASK_COLUMN, MASK_FEATURE, MASK_NEIGHBOR
+    from .tokens import _order16
+    key = {MASK_COLUMN: "col_perm", MASK_FEATURE: "out_perm", MASK_NEIGHBOR: "in_perm"}
+    out = []
+    for kind in kinds:
+        if kind in key:
+            order = _order16(meta[key[kind]])
+        else:
+            b, s = meta["seq_row_ids"].shape
+            order = torch.arange(s, device=meta["seq_row_ids"].device, dtype=torch.int32).to(torch.int16)
+            order = order.expand(b, s).contiguous()
+        plan = rt.build_tile_plan(order, meta["seq_row_ids"], meta["column_ids"], meta["is_padding"],
+                                  meta["fk_adj"], kind, max_rows=max_rows)
+        out.append((order, plan))
+    return out
