@@ -546,6 +546,16 @@ def run_train_arm(args, cfg):
         raise RuntimeError(f"device status {status}, loss {loss_val}")
     tokens = cfg["B"] * cfg["S"]
     flops, attn_flops = train_flops(model, cfg, build_masks(d, TRAIN_KINDS), tokens)
+    # replicas must stay identical: same initial weights, same averaged gradients
+    with torch.no_grad():
+        chk = torch.stack([p.double().sum() for p in model.parameters()]).sum().reshape(1)
+    drift = 0.0
+    if world > 1:
+        import torch.distributed as dist
+        allc = [torch.zeros_like(chk) for _ in range(world)]
+        dist.all_gather(allc, chk)
+        vals = torch.cat(allc)
+        drift = float((vals.max() - vals.min()).abs() / vals.abs().max().clamp_min(1e-30))
     peak_tf, _, peak_src = measured_peaks()
     achieved = flops / (step_ms * 1e-3) / 1e12
     n_params = sum(p.numel() for p in model.parameters())
@@ -570,6 +580,7 @@ def run_train_arm(args, cfg):
             "gpu_launches": args.steps * (10 + cfg["layers"] * len(TRAIN_KINDS) * 5),
             "clocks": clocks,
             "final_loss": loss_val,
+            "replica_param_checksum_rel_spread": drift,
         }
         if not args.no_cpu_baseline:
             v, sample = train_cpu_sample(cfg, args.cpu_seconds)
