@@ -376,8 +376,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // columns [32g, 32g+16) as bf16 pairs, one run per 32-column slice g), dP^T
 // [256,384) fp32 (dS^T likewise), dV [384,384+DH), dK [384+DH,384+2DH).
 // Sixteen softmax warps: four per TMEM lane quadrant, each owning 32 columns.
-// Per q-tile i: dV_i and S^T_{i+1} follow softmax phase A (overlapping phase
-// B), dK_i and dP^T_{i+1} follow phase B (overlapping the next phase A).
+// Per q-tile i: S^T_{i+1} then dV_i follow softmax phase A (overlapping phase
+// B and the next phase A), dK_i and dP^T_{i+1} follow phase B.
 // ---------------------------------------------------------------------------
 template <int DH>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -472,17 +472,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; ok && i < n_tiles; ++i) {
         if (!(ok = mbar_wait(&bars.pa_full, i & 1, &abort_flag))) break;
         tc_fence_after();
-#pragma unroll
-        for (int ks = 0; ks < RT_TILE / 16; ++ks)  // dV += P^T_i dO_i
-          mma_ts(tmem + kDV, tmem + kST0 + (i & 1) * 128 + packed_col(ks),
-                 sdesc(do_addr(i) + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_g,
-                 (i > 0 || ks > 0) ? 1u : 0u);
+        // S^T_{i+1} first: the softmax warps start its phase A while dV_i
+        // runs (MMA issue blocks for the MMA's duration, so issuing dV_i
+        // first would put it on the softmax's critical path). S^T_{i+1}
+        // targets the other buffer; dV_i reads P^T_i from this one.
         if (i + 1 < n_tiles) {
           if (!(ok = mbar_wait(&bars.ring_full[(i + 1) % C::kStages], ((i + 1) / C::kStages) & 1, &abort_flag)))
             break;
           tc_fence_after();
           issue_st(i + 1);
         }
+#pragma unroll
+        for (int ks = 0; ks < RT_TILE / 16; ++ks)  // dV += P^T_i dO_i
+          mma_ts(tmem + kDV, tmem + kST0 + (i & 1) * 128 + packed_col(ks),
+                 sdesc(do_addr(i) + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_g,
+                 (i > 0 || ks > 0) ? 1u : 0u);
         if (!(ok = mbar_wait(&bars.pb_full, i & 1, &abort_flag))) break;
         tc_fence_after();
 #pragma unroll
