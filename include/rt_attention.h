@@ -165,7 +165,9 @@ int rt_attention_fwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, in
                      const rt_tile_plan* plan, uint16_t* o, float* lse, void* stream);
 
 /* Workspace for the backward: [batch*heads][2][seq_len rounded up to 128]
- * fp32 -- lse (log2 units) and rowsum(dO * O) per query, zero past seq_len. */
+ * fp32 -- lse (log2 units) and rowsum(dO * O) per query, zero past seq_len --
+ * then the fp32 dQ accumulator [batch*heads][seq_len rounded up][64] of the
+ * fused dK/dV/dQ pass. */
 size_t rt_attention_bwd_workspace_bytes(int32_t batch, int32_t heads, int32_t seq_len);
 
 /* Backward: the gradients jax autodiff takes through layers.py:83-94.

@@ -41,6 +41,15 @@ struct Cfg {
   // 512 TMEM columns per CTA: ask for enough shared memory that a second CTA
   // never lands on the same SM (it would only block in tcgen05.alloc).
   static constexpr int kDynSmem = (kSmemBytes + 1024) > 118 * 1024 ? (kSmemBytes + 1024) : 118 * 1024;
+  // fused dK/dV/dQ kernel: a dS^T tile [2 panels][128 keys][64 queries] bf16 after the stats ring
+  static constexpr int kDS = (kSmemBytes + 1023) & ~1023;
+  static constexpr int kDSPanel = RT_TILE * 128;
+  // then the dQ staging tile: DH / 32 boxes of [128 rows][32 fp32] with the 128-byte swizzle
+  static constexpr int kStg = kDS + 2 * kDSPanel;
+  static constexpr int kStgBox = RT_TILE * 128;
+  static constexpr int kStgBytes = (DH / 32) * kStgBox;
+  static constexpr int kDynSmemFused =
+      (kStg + kStgBytes + 1024) > 118 * 1024 ? (kStg + kStgBytes + 1024) : 118 * 1024;
 };
 
 constexpr int kMaxTiles = 65536 / RT_TILE;
@@ -54,6 +63,9 @@ struct __align__(8) Barriers {
   uint64_t pa_full;        // softmax phase A done: S buffer read (and P^T written)
   uint64_t pb_full;        // softmax phase B done: dS (or dS^T) written
   uint64_t done;           // last gradient MMA complete
+  uint64_t dq_ready;       // fused kernel: dQ partial of the tile in TMEM
+  uint64_t stg_full;       // fused kernel: dQ staging tile written (softmax warps)
+  uint64_t stg_free;       // fused kernel: previous TMA reduce has read the staging tile
   uint64_t drain;
 };
 
@@ -69,6 +81,9 @@ __device__ __forceinline__ void init_barriers(Barriers& bars, int stages) {
   mbar_init(&bars.pa_full, kSoftmaxThreads / 32);  // one arrival per softmax warp
   mbar_init(&bars.pb_full, kSoftmaxThreads / 32);
   mbar_init(&bars.done, 1);
+  mbar_init(&bars.dq_ready, 1);
+  mbar_init(&bars.stg_full, kSoftmaxThreads / 32);
+  mbar_init(&bars.stg_free, 1);
   mbar_init(&bars.drain, 1);
   fence_mbar_init();
 }
@@ -134,6 +149,33 @@ __device__ __forceinline__ void softmax_phase_b(uint32_t taddr, const uint32_t (
     ds[(e >> 1) + 1] = pack_bf16x2(g23.x, g23.y);
   }
   tmem_st16(taddr, ds);
+}
+
+// Phase B math only: dS = P * (dP - delta) from the 32 dP columns at `taddr`,
+// returned as 16 bf16 pairs.
+template <bool kPerColumn>
+__device__ __forceinline__ void softmax_phase_b_ds(uint32_t taddr, const uint32_t (&pk)[16], const float* nd_col,
+                                                   float nd_row, uint32_t (&ds)[16]) {
+  uint32_t d[32];
+  tmem_ld32(taddr, d);
+  tmem_wait_ld();
+#pragma unroll
+  for (int e = 0; e < 32; e += 4) {
+    float2 nd01, nd23;
+    if (kPerColumn) {
+      const float4 v = *reinterpret_cast<const float4*>(nd_col + e);
+      nd01 = make_float2(v.x, v.y);
+      nd23 = make_float2(v.z, v.w);
+    } else {
+      nd01 = nd23 = make_float2(nd_row, nd_row);
+    }
+    const float2 g01 = fmul2(unpack_bf16x2(pk[e >> 1]),
+                             fadd2(make_float2(__uint_as_float(d[e]), __uint_as_float(d[e + 1])), nd01));
+    const float2 g23 = fmul2(unpack_bf16x2(pk[(e >> 1) + 1]),
+                             fadd2(make_float2(__uint_as_float(d[e + 2]), __uint_as_float(d[e + 3])), nd23));
+    ds[e >> 1] = pack_bf16x2(g01.x, g01.y);
+    ds[(e >> 1) + 1] = pack_bf16x2(g23.x, g23.y);
+  }
 }
 
 // TMEM column of the bf16 P / dS operand for MMA k-step ks (16 rows of the
@@ -568,10 +610,299 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Fused dK, dV and dQ: one CTA per (b, h, k-tile), dkdv_kernel's pipeline plus
+// dQ, so S, dP and P are computed once per live tile instead of twice.
+// Phase B writes dS^T (bf16) to a shared-memory tile [2 panels][128 keys][64
+// queries] with the 128-byte swizzle instead of TMEM. The MMAs read it twice:
+// as dS^T, K-major (dK += dS^T Q_i), and as dS, MN-major over both panels
+// (dQ_i = dS K, M = the 128 queries). dQ_i lands over columns [0, DH) of the
+// S^T buffer that dV_i has just consumed. Before arriving on phase A of the
+// next tile the softmax warps copy it into a shared staging tile (the 128-byte
+// swizzle, conflict-free), and the first softmax thread reduce-adds the tile
+// into the fp32 accumulator dq_acc [B*H][S padded][DH] with TMA
+// (cp.reduce.async.bulk.tensor, whole 128-byte lines); dq_convert_kernel
+// scales and rounds it afterwards. Every dQ row block gets one partial per
+// live key tile in an order the memory system decides, so dQ is reproducible
+// to fp32 rounding; dK and dV are written once.
+// TMEM as dkdv_kernel: S^T0 [0,128), S^T1 [128,256), dP^T [256,384), dV, dK.
+// ---------------------------------------------------------------------------
+template <int DH>
+__global__ void __launch_bounds__(kThreads, 1)
+    dkdvq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                const rt_tile_plan plan, int H, int S, float scale, float scale_log2,
+                const float* __restrict__ stats, uint16_t* __restrict__ dk, uint16_t* __restrict__ dv,
+                const __grid_constant__ CUtensorMap tm_acc) {
+  using C = Cfg<DH>;
+  constexpr int kST0 = 0, kDPT = 256, kDV = 384, kDK = 384 + DH;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ Barriers bars;
+  __shared__ uint32_t tmem_base_s;
+  __shared__ int abort_flag;
+  __shared__ int s_list[kMaxTiles];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int T = plan.tiles;
+  const int bh = b * H + h;
+  const int col_list = b * T + kt;
+  const int list_begin = plan.k2q_ptr[col_list];
+  const int n_tiles = plan.k2q_ptr[col_list + 1] - list_begin;
+  const int Sp = T * RT_TILE;
+  for (int i = threadIdx.x; i < n_tiles; i += kThreads) s_list[i] = plan.k2q_idx[list_begin + i];
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    init_barriers(bars, C::kStages);
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base_s, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_s;
+
+  if (warp == 0) {
+    if (lane == 0 && n_tiles > 0) {
+      mbar_arrive_expect_tx(&bars.res_full, 2 * C::kTileBytes);
+      tma_load_3d(smem + C::kA0, &tm_k, &bars.res_full, 0, kt * RT_TILE, bh);
+      tma_load_3d(smem + C::kA1, &tm_v, &bars.res_full, 0, kt * RT_TILE, bh);
+      int i = 0;
+      for (; i < n_tiles; ++i) {
+        const int s = i % C::kStages;
+        if (i >= C::kStages && !mbar_wait(&bars.ring_empty[s], ((i / C::kStages) - 1) & 1, &abort_flag)) break;
+        const int qtile = s_list[i] & 0x7FFFFFFF;
+        mbar_arrive_expect_tx(&bars.ring_full[s], 2 * C::kTileBytes + C::kRowStatBytes);
+        tma_load_3d(smem + C::kR0 + s * C::kTileBytes, &tm_q, &bars.ring_full[s], 0, qtile * RT_TILE, bh);
+        tma_load_3d(smem + C::kR1 + s * C::kTileBytes, &tm_do, &bars.ring_full[s], 0, qtile * RT_TILE, bh);
+        uint8_t* st = smem + C::kRL + s * C::kRowStatBytes;
+        const float* src = stats + (size_t)bh * 2 * Sp + (size_t)qtile * RT_TILE;
+        bulk_load(st, src, RT_TILE * 4, &bars.ring_full[s]);
+        bulk_load(st + RT_TILE * 4, src + Sp, RT_TILE * 4, &bars.ring_full[s]);
+      }
+      volatile int no_abort = 0;
+      for (int ii = max(0, i - C::kStages); ii < i; ++ii)
+        mbar_wait(&bars.ring_full[ii % C::kStages], (ii / C::kStages) & 1, &no_abort);
+      mbar_wait(&bars.res_full, 0, &no_abort);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n_tiles > 0) {
+      constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false, false);
+      constexpr uint32_t idesc_g = idesc_bf16_f32(128, DH, false, true);
+      constexpr uint32_t idesc_dq = idesc_bf16_f32(128, DH, true, true);
+      const uint32_t ds_addr = smem_u32(smem + C::kDS);
+      const uint32_t k_addr = smem_u32(smem + C::kA0);
+      const uint32_t v_addr = smem_u32(smem + C::kA1);
+      auto q_addr = [&](int i) { return smem_u32(smem + C::kR0 + (i % C::kStages) * C::kTileBytes); };
+      auto do_addr = [&](int i) { return smem_u32(smem + C::kR1 + (i % C::kStages) * C::kTileBytes); };
+      auto issue_st = [&](int i) {  // S^T[i%2] = K Q_i^T
+#pragma unroll
+        for (int ks = 0; ks < DH / 16; ++ks)
+          mma_ss(tmem + kST0 + (i & 1) * 128, sdesc(k_addr + ks * 32, 16, C::kSBO, C::kSwizzle),
+                 sdesc(q_addr(i) + ks * 32, 16, C::kSBO, C::kSwizzle), idesc_s, ks > 0 ? 1u : 0u);
+        mma_commit(&bars.st_full[i & 1]);
+      };
+      auto issue_dpt = [&](int i) {  // dP^T = V dO_i^T
+#pragma unroll
+        for (int ks = 0; ks < DH / 16; ++ks)
+          mma_ss(tmem + kDPT, sdesc(v_addr + ks * 32, 16, C::kSBO, C::kSwizzle),
+                 sdesc(do_addr(i) + ks * 32, 16, C::kSBO, C::kSwizzle), idesc_s, ks > 0 ? 1u : 0u);
+        mma_commit(&bars.dp_full);
+      };
+      bool ok = mbar_wait(&bars.res_full, 0, &abort_flag) && mbar_wait(&bars.ring_full[0], 0, &abort_flag);
+      tc_fence_after();
+      if (ok) {
+        issue_st(0);
+        issue_dpt(0);
+      }
+      // S^T_{i+1} is issued only once phase A of tile i has been observed, so
+      // no barrier can run two phases ahead of its waiter.
+      for (int i = 0; ok && i < n_tiles; ++i) {
+        if (!(ok = mbar_wait(&bars.pa_full, i & 1, &abort_flag))) break;
+        tc_fence_after();
+        // S^T_{i+1} first: the softmax warps start its phase A while dV_i
+        // runs (MMA issue blocks for the MMA's duration, so issuing dV_i
+        // first would put it on the softmax's critical path). S^T_{i+1}
+        // targets the other buffer; dV_i reads P^T_i from this one.
+        if (i + 1 < n_tiles) {
+          if (!(ok = mbar_wait(&bars.ring_full[(i + 1) % C::kStages], ((i + 1) / C::kStages) & 1, &abort_flag)))
+            break;
+          tc_fence_after();
+          issue_st(i + 1);
+        }
+#pragma unroll
+        for (int ks = 0; ks < RT_TILE / 16; ++ks)  // dV += P^T_i dO_i
+          mma_ts(tmem + kDV, tmem + kST0 + (i & 1) * 128 + packed_col(ks),
+                 sdesc(do_addr(i) + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_g,
+                 (i > 0 || ks > 0) ? 1u : 0u);
+        if (!(ok = mbar_wait(&bars.pb_full, i & 1, &abort_flag))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < RT_TILE / 16; ++ks)  // dK += dS^T_i Q_i (A: dS^T tile, K-major)
+          mma_ss(tmem + kDK, sdesc(ds_addr + (ks >> 2) * C::kDSPanel + (ks & 3) * 32, 16, 1024, SW_128B),
+                 sdesc(q_addr(i) + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_g,
+                 (i > 0 || ks > 0) ? 1u : 0u);
+#pragma unroll
+        for (int ks = 0; ks < RT_TILE / 16; ++ks)  // dQ_i = dS K (A: the same tile, MN-major over both panels)
+          mma_ss(tmem + kST0 + (i & 1) * 128, sdesc(ds_addr + ks * 16 * 128, C::kDSPanel, 1024, SW_128B),
+                 sdesc(k_addr + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_dq, ks > 0 ? 1u : 0u);
+        mma_commit(&bars.dq_ready);
+        mma_commit(&bars.ring_empty[i % C::kStages]);
+        if (i + 1 < n_tiles) issue_dpt(i + 1);
+      }
+      mma_commit(&bars.done);
+      mma_commit(&bars.drain);
+      volatile int no_abort = 0;
+      mbar_wait(&bars.drain, 0, &no_abort);
+    }
+  } else {
+    const int quad = warp & 3;
+    const int grp = (warp - 2) >> 2;  // column group: queries [32 grp, 32 grp + 32) of every tile
+    const int row = quad * 32 + lane;  // key within the tile
+    const int key = kt * RT_TILE + row;
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+    const uint32_t col0 = (uint32_t)(grp * 32);
+    const uint32_t* masks_t = plan.tile_masks_t + ((size_t)col_list * T) * RT_TILE * 4 + grp;
+    auto load_mask = [&](int ent) {
+      return ent >= 0 ? __ldg(masks_t + ((size_t)(ent & 0x7FFFFFFF) * RT_TILE + row) * 4) : 0xFFFFFFFFu;
+    };
+    // dQ partial of tile t (queries of q-tile s_list[t] in TMEM lanes = rows):
+    // this warp copies columns [16 grp, 16 grp + 16) of its 32 rows into the
+    // staging tile; the first softmax thread then reduce-adds the whole tile
+    // into dq_acc (TMA), and, before the next drain rewrites the tile, waits
+    // for that reduce to have read it.
+    const bool leader_warp = warp == 2;
+    auto drain_dq = [&](int t) -> bool {
+      if (!mbar_wait_warp(&bars.dq_ready, t & 1, &abort_flag)) return false;
+      tc_fence_after();
+      const bool has = grp * 16 < DH;
+      uint32_t r[16];
+      if (has) {
+        tmem_ld16(lane_base + kST0 + (t & 1) * 128 + grp * 16, r);
+        tmem_wait_ld();
+      }
+      if (t > 0) {
+        if (leader_warp && lane == 0) {
+          bulk_wait_read_all();
+          mbar_arrive(&bars.stg_free);
+        }
+        if (!mbar_wait_warp(&bars.stg_free, (t - 1) & 1, &abort_flag)) return false;
+      }
+      if (has) {
+        uint8_t* box = smem + C::kStg + (grp >> 1) * C::kStgBox + row * 128;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int chunk = (grp & 1) * 4 + c;
+          *reinterpret_cast<uint4*>(box + ((chunk ^ (row & 7)) << 4)) =
+              make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive_warp(&bars.stg_full);
+      if (leader_warp) {
+        if (!mbar_wait_warp(&bars.stg_full, t & 1, &abort_flag)) return false;
+        if (lane == 0) {
+          const int row0 = bh * Sp + (s_list[t] & 0x7FFFFFFF) * RT_TILE;
+#pragma unroll
+          for (int x = 0; x < DH / 32; ++x) tma_reduce_add_2d(&tm_acc, smem + C::kStg + x * C::kStgBox, x * 32, row0);
+          bulk_commit_group();
+        }
+        __syncwarp();
+      }
+      return true;
+    };
+    uint32_t mk_next = n_tiles > 0 ? load_mask(s_list[0]) : 0u;
+    bool ok = true;
+    for (int i = 0; i < n_tiles; ++i) {
+      const bool full = s_list[i] < 0;
+      const uint32_t mk = mk_next;
+      if (i + 1 < n_tiles) mk_next = load_mask(s_list[i + 1]);
+      const int stage = i % C::kStages;
+      if (!(ok = mbar_wait_warp(&bars.ring_full[stage], (i / C::kStages) & 1, &abort_flag))) break;
+      const float* nl = reinterpret_cast<const float*>(smem + C::kRL + stage * C::kRowStatBytes) + col0;
+      const float* nd = nl + RT_TILE;
+      if (!(ok = mbar_wait_warp(&bars.st_full[i & 1], (i >> 1) & 1, &abort_flag))) break;
+      tc_fence_after();
+      uint32_t pk[16];
+      const uint32_t st_addr = lane_base + kST0 + (i & 1) * 128 + col0;
+      softmax_phase_a<true>(st_addr, full, mk, scale_log2, nl, 0.f, pk);
+      tmem_st16(st_addr, pk);  // P^T over the first 16 columns of this slice
+      tmem_wait_st();
+      if (i > 0 && !(ok = drain_dq(i - 1))) break;
+      tc_fence_before();
+      mbar_arrive_warp(&bars.pa_full);
+      if (!(ok = mbar_wait_warp(&bars.dp_full, i & 1, &abort_flag))) break;
+      tc_fence_after();
+      uint32_t ds[16];
+      softmax_phase_b_ds<true>(lane_base + kDPT + col0, pk, nd, 0.f, ds);
+      // dS^T row `row`, queries [32 grp, 32 grp + 32): panel grp / 2, 16-byte
+      // chunks (grp % 2) * 4 + c of the row, stored at chunk ^ (row % 8)
+      uint8_t* drow = smem + C::kDS + (grp >> 1) * C::kDSPanel + row * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int chunk = (grp & 1) * 4 + c;
+        *reinterpret_cast<uint4*>(drow + ((chunk ^ (row & 7)) << 4)) =
+            make_uint4(ds[4 * c], ds[4 * c + 1], ds[4 * c + 2], ds[4 * c + 3]);
+      }
+      fence_proxy_async_smem();  // the tensor core reads the tile through the async proxy
+      tc_fence_before();
+      mbar_arrive_warp(&bars.pb_full);
+    }
+    if (ok && n_tiles > 0) ok = drain_dq(n_tiles - 1);
+    if (leader_warp && lane == 0) bulk_wait_all();  // every reduce issued has completed
+    if (ok && n_tiles > 0 && mbar_wait_warp(&bars.done, 0, &abort_flag)) {
+      tc_fence_after();
+      uint16_t* dst_v = dv + ((size_t)bh * S + key) * DH;
+      uint16_t* dst_k = dk + ((size_t)bh * S + key) * DH;
+#pragma unroll
+      for (int c = grp * EpiSlice<DH>::kCols; c < (grp + 1) * EpiSlice<DH>::kCols && c < DH; c += 16) {
+        uint32_t r[16], pko[8];
+        tmem_ld16(lane_base + kDV + c, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) pko[e / 2] = pack_bf16x2(__uint_as_float(r[e]), __uint_as_float(r[e + 1]));
+        if (key < S) store_row_bf16(dst_v + c, pko);
+        tmem_ld16(lane_base + kDK + c, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; e += 2)
+          pko[e / 2] = pack_bf16x2(__uint_as_float(r[e]) * scale, __uint_as_float(r[e + 1]) * scale);
+        if (key < S) store_row_bf16(dst_k + c, pko);
+      }
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// dQ = scale * dq_acc, rounded to bf16, for the seq_len real rows of each (b, h).
+template <int DH>
+__global__ void __launch_bounds__(256) dq_convert_kernel(const float* __restrict__ dq_acc, uint16_t* __restrict__ dq,
+                                                         long long rows, int S, int Sp, float scale) {
+  const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // 8 elements each
+  const long long row = gid / (DH / 8);
+  if (row >= rows) return;
+  const int c = (int)(gid % (DH / 8)) * 8;
+  const long long bh = row / S;
+  const int q = (int)(row % S);
+  const float4* src = reinterpret_cast<const float4*>(dq_acc + ((size_t)bh * Sp + q) * DH + c);
+  const float4 a = src[0], b = src[1];
+  *reinterpret_cast<uint4*>(dq + (size_t)row * DH + c) =
+      make_uint4(pack_bf16x2(a.x * scale, a.y * scale), pack_bf16x2(a.z * scale, a.w * scale),
+                 pack_bf16x2(b.x * scale, b.y * scale), pack_bf16x2(b.z * scale, b.w * scale));
+}
+
 template <int DH>
 int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* o, const uint16_t* d_o,
            const float* lse, int B, int H, int S, float scale, const rt_tile_plan& plan, uint16_t* dq,
-           uint16_t* dk, uint16_t* dv, float* stats, cudaStream_t stream) {
+           uint16_t* dk, uint16_t* dv, float* stats, float* dq_acc, cudaStream_t stream) {
   using C = Cfg<DH>;
   CUtensorMap tq, tk, tv, tdo;
   if (make_qkv_tensor_map(&tq, q, B * H, S, DH) != RT_OK || make_qkv_tensor_map(&tk, k, B * H, S, DH) != RT_OK ||
@@ -585,6 +916,8 @@ int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16
     if (e != cudaSuccess) return cuda_failure(e, "cudaFuncSetAttribute(dq_kernel)");
     e = cudaFuncSetAttribute(dkdv_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kDynSmem);
     if (e != cudaSuccess) return cuda_failure(e, "cudaFuncSetAttribute(dkdv_kernel)");
+    e = cudaFuncSetAttribute(dkdvq_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kDynSmemFused);
+    if (e != cudaSuccess) return cuda_failure(e, "cudaFuncSetAttribute(dkdvq_kernel)");
     configured[dev] = true;
   }
   const int Sp = plan.tiles * RT_TILE;
@@ -595,6 +928,19 @@ int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16
   if (int st = check_launch("row_stats_kernel launch")) return st;
   const float scale_log2 = scale * 1.4426950408889634f;
   dim3 grid(plan.tiles, H, B);
+  if (dq_acc != nullptr) {  // fused: one pass for dK, dV and dQ
+    cudaError_t e = cudaMemsetAsync(dq_acc, 0, sizeof(float) * (size_t)rows_padded * DH, stream);
+    if (e != cudaSuccess) return cuda_failure(e, "cudaMemsetAsync(dq accumulator)");
+    CUtensorMap tacc;
+    if (make_acc_tensor_map(&tacc, dq_acc, rows_padded, DH) != RT_OK) return RT_ERR_CUDA;
+    dkdvq_kernel<DH><<<grid, kThreads, C::kDynSmemFused, stream>>>(tq, tk, tv, tdo, plan, H, S, scale, scale_log2,
+                                                                   stats, dk, dv, tacc);
+    if (int st = check_launch("dkdvq_kernel launch")) return st;
+    const long long rows = (long long)B * H * S;
+    const long long cthreads = rows * (DH / 8);
+    dq_convert_kernel<DH><<<(unsigned)((cthreads + 255) / 256), 256, 0, stream>>>(dq_acc, dq, rows, S, Sp, scale);
+    return check_launch("dq_convert_kernel launch");
+  }
   dkdv_kernel<DH><<<grid, kThreads, C::kDynSmem, stream>>>(tq, tk, tv, tdo, plan, H, S, scale, scale_log2,
                                                             stats, dk, dv);
   if (int st = check_launch("dkdv_kernel launch")) return st;
@@ -608,9 +954,11 @@ int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16
 int launch_attention_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* o,
                          const uint16_t* d_o, const float* lse, int B, int H, int S, int Dh, float scale,
                          const rt_tile_plan& plan, uint16_t* dq, uint16_t* dk, uint16_t* dv, float* stats,
-                         cudaStream_t stream) {
-  if (Dh == 64) return bwd::launch<64>(q, k, v, o, d_o, lse, B, H, S, scale, plan, dq, dk, dv, stats, stream);
-  if (Dh == 32) return bwd::launch<32>(q, k, v, o, d_o, lse, B, H, S, scale, plan, dq, dk, dv, stats, stream);
+                         float* dq_acc, cudaStream_t stream) {
+  if (Dh == 64)
+    return bwd::launch<64>(q, k, v, o, d_o, lse, B, H, S, scale, plan, dq, dk, dv, stats, dq_acc, stream);
+  if (Dh == 32)
+    return bwd::launch<32>(q, k, v, o, d_o, lse, B, H, S, scale, plan, dq, dk, dv, stats, dq_acc, stream);
   return RT_ERR_UNSUPPORTED;
 }
 
