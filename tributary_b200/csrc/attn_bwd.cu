@@ -740,16 +740,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                  (i > 0 || ks > 0) ? 1u : 0u);
         if (!(ok = mbar_wait(&bars.pb_full, i & 1, &abort_flag))) break;
         tc_fence_after();
+        // dQ_i first: its drain precedes the softmax's next phase-A arrival,
+        // which the next S^T / dV wait for; dK_i is not waited on until the end
 #pragma unroll
-        for (int ks = 0; ks < RT_TILE / 16; ++ks)  // dK += dS^T_i Q_i (A: dS^T tile, K-major)
-          mma_ss(tmem + kDK, sdesc(ds_addr + (ks >> 2) * C::kDSPanel + (ks & 3) * 32, 16, 1024, SW_128B),
-                 sdesc(q_addr(i) + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_g,
-                 (i > 0 || ks > 0) ? 1u : 0u);
-#pragma unroll
-        for (int ks = 0; ks < RT_TILE / 16; ++ks)  // dQ_i = dS K (A: the same tile, MN-major over both panels)
+        for (int ks = 0; ks < RT_TILE / 16; ++ks)  // dQ_i = dS K (A: the dS^T tile read MN-major over both panels)
           mma_ss(tmem + kST0 + (i & 1) * 128, sdesc(ds_addr + ks * 16 * 128, C::kDSPanel, 1024, SW_128B),
                  sdesc(k_addr + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_dq, ks > 0 ? 1u : 0u);
         mma_commit(&bars.dq_ready);
+#pragma unroll
+        for (int ks = 0; ks < RT_TILE / 16; ++ks)  // dK += dS^T_i Q_i (A: the same tile, K-major)
+          mma_ss(tmem + kDK, sdesc(ds_addr + (ks >> 2) * C::kDSPanel + (ks & 3) * 32, 16, 1024, SW_128B),
+                 sdesc(q_addr(i) + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_g,
+                 (i > 0 || ks > 0) ? 1u : 0u);
         mma_commit(&bars.ring_empty[i % C::kStages]);
         if (i + 1 < n_tiles) issue_dpt(i + 1);
       }
