@@ -44,10 +44,16 @@ __global__ void fk_pack_kernel(const uint8_t* __restrict__ fk_adj, int R, int WR
   }
 }
 
+// One CTA per (b, q-tile, k-tile), one query row per thread; KIND is a
+// template parameter so the element loop carries no per-element branch on it.
+// The warp walks the keys in lockstep, and in the sampler's row orders the
+// keys of a tile come in runs of one row, so the fk word a key needs is
+// cached per thread and reloaded only when the row's word changes.
+template <int KIND>
 __global__ void __launch_bounds__(128) tile_mask_kernel(
     const uint16_t* __restrict__ perm, const uint16_t* __restrict__ seq_row_ids,
     const int32_t* __restrict__ column_ids, const uint8_t* __restrict__ is_padding,
-    const uint32_t* __restrict__ fk_bits, int S, int R, int WR, int kind, rt_tile_plan plan) {
+    const uint32_t* __restrict__ fk_bits, int S, int R, int WR, rt_tile_plan plan) {
   const int kt = blockIdx.x;
   const int qt = blockIdx.y;
   const int b = blockIdx.z;
@@ -94,6 +100,8 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
   __syncthreads();
 
   uint32_t w4[4];
+  int cached_w = -1;  // fk word index held in cached_bits (warp-uniform: all lanes see the same key)
+  uint32_t cached_bits = 0;
 #pragma unroll
   for (int w = 0; w < 4; ++w) {
     uint32_t word = 0;
@@ -106,14 +114,19 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
         if (pj >= 0) {
           const bool valid = !padi && !s_kpad[j];
           bool rel;
-          if (kind == RT_MASK_COLUMN) {
+          if (KIND == RT_MASK_COLUMN) {
             rel = ci == s_kcol[j];
-          } else if (kind == RT_MASK_FEATURE) {
+          } else if (KIND == RT_MASK_FEATURE || KIND == RT_MASK_NEIGHBOR) {
             const int rj = s_krow[j];
-            rel = (ri == rj) || (fkrow != nullptr && ((__ldg(fkrow + (rj >> 5)) >> (rj & 31)) & 1u));
-          } else if (kind == RT_MASK_NEIGHBOR) {
-            const int rj = s_krow[j];
-            rel = fkrow != nullptr && ((__ldg(fkrow + (rj >> 5)) >> (rj & 31)) & 1u);
+            uint32_t fk = 0u;
+            if (fkrow != nullptr) {
+              if ((rj >> 5) != cached_w) {
+                cached_w = rj >> 5;
+                cached_bits = __ldg(fkrow + cached_w);
+              }
+              fk = (cached_bits >> (rj & 31)) & 1u;
+            }
+            rel = (KIND == RT_MASK_FEATURE && ri == rj) || fk != 0u;
           } else {
             rel = true;
           }
@@ -248,8 +261,19 @@ int launch_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids, co
                                                   plan.fk_bits);
     fk_bits = plan.fk_bits;
   }
-  tile_mask_kernel<<<dim3(T, T, B), RT_TILE, 0, stream>>>(perm, seq_row_ids, column_ids, is_padding,
-                                                           fk_bits, S, R, WR, kind, plan);
+  const dim3 grid(T, T, B);
+  if (kind == RT_MASK_COLUMN)
+    tile_mask_kernel<RT_MASK_COLUMN><<<grid, RT_TILE, 0, stream>>>(perm, seq_row_ids, column_ids, is_padding,
+                                                                   fk_bits, S, R, WR, plan);
+  else if (kind == RT_MASK_FEATURE)
+    tile_mask_kernel<RT_MASK_FEATURE><<<grid, RT_TILE, 0, stream>>>(perm, seq_row_ids, column_ids, is_padding,
+                                                                    fk_bits, S, R, WR, plan);
+  else if (kind == RT_MASK_NEIGHBOR)
+    tile_mask_kernel<RT_MASK_NEIGHBOR><<<grid, RT_TILE, 0, stream>>>(perm, seq_row_ids, column_ids, is_padding,
+                                                                     fk_bits, S, R, WR, plan);
+  else
+    tile_mask_kernel<RT_MASK_FULL><<<grid, RT_TILE, 0, stream>>>(perm, seq_row_ids, column_ids, is_padding,
+                                                                 fk_bits, S, R, WR, plan);
   tile_list_kernel<<<1, 1024, 0, stream>>>(plan);
   return check_launch("tile plan kernels launch");
 }
