@@ -167,7 +167,8 @@ int rt_attention_fwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, in
 /* Workspace for the backward: [batch*heads][2][seq_len rounded up to 128]
  * fp32 -- lse (log2 units) and rowsum(dO * O) per query, zero past seq_len --
  * then the fp32 dQ accumulator [batch*heads][seq_len rounded up][64] of the
- * fused dK/dV/dQ pass. */
+ * fused dK/dV/dQ pass, then that pass's row-statistic operand rows
+ * [batch*heads][seq_len rounded up][16] bf16. */
 size_t rt_attention_bwd_workspace_bytes(int32_t batch, int32_t heads, int32_t seq_len);
 
 /* Backward: the gradients jax autodiff takes through layers.py:83-94.

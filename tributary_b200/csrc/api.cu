@@ -157,19 +157,34 @@ int make_qkv_tensor_map(CUtensorMap* map, const void* base, int BH, int S, int D
   return r == CUDA_SUCCESS ? RT_OK : driver_failure((int)r, "cuTensorMapEncodeTiled");
 }
 
-// fp32 accumulator [rows][Dh] as boxes of 128 rows x 32 floats (128 B, the
-// widest box the 128-byte swizzle allows), for TMA reduce-adds.
+// fp32 accumulator [rows][Dh] as boxes of 128 rows x 16 floats (64 B rows,
+// the 64-byte swizzle), for the TMA reduce-adds of the fused backward.
 int make_acc_tensor_map(CUtensorMap* map, float* base, long long rows, int Dh) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return driver_failure(-1, "cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)");
   cuuint64_t dims[2] = {(cuuint64_t)Dh, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)Dh * 4};
-  cuuint32_t box[2] = {32, (cuuint32_t)RT_TILE};
+  cuuint32_t box[2] = {16, (cuuint32_t)RT_TILE};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? RT_OK : driver_failure((int)r, "cuTensorMapEncodeTiled(dq accumulator)");
+}
+
+// Row-statistic operand rows [rows][16] bf16 (32 B each) as boxes of 128 rows
+// with the 32-byte swizzle: one K-major MMA operand tile per box.
+int make_aux_tensor_map(CUtensorMap* map, uint16_t* base, long long rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return driver_failure(-1, "cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)");
+  cuuint64_t dims[2] = {16, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {32};
+  cuuint32_t box[2] = {16, (cuuint32_t)RT_TILE};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? RT_OK : driver_failure((int)r, "cuTensorMapEncodeTiled(row statistics)");
 }
 
 }  // namespace rt
@@ -266,7 +281,8 @@ size_t bwd_stats_bytes(int32_t batch, int32_t heads, int32_t seq_len) {
 size_t rt_attention_bwd_workspace_bytes(int32_t batch, int32_t heads, int32_t seq_len) {
   if (batch < 0 || heads < 0 || seq_len < 0) return 0;
   const size_t padded = (size_t)((seq_len + RT_TILE - 1) / RT_TILE) * RT_TILE;
-  return bwd_stats_bytes(batch, heads, seq_len) + align_up(64 * sizeof(float) * (size_t)batch * heads * padded);
+  const size_t rows = (size_t)batch * heads * padded;
+  return bwd_stats_bytes(batch, heads, seq_len) + align_up(64 * sizeof(float) * rows) + align_up(32 * rows);
 }
 
 int rt_attention_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* o,
@@ -288,10 +304,12 @@ int rt_attention_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, co
   DeviceGuard guard(q);
   if (guard.status() != RT_OK) return guard.status();
   float* stats = static_cast<float*>(workspace);
-  float* dq_acc = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
-                                           bwd_stats_bytes(batch, heads, seq_len));
+  const size_t padded = (size_t)((seq_len + RT_TILE - 1) / RT_TILE) * RT_TILE;
+  uint8_t* acc_base = static_cast<uint8_t*>(workspace) + bwd_stats_bytes(batch, heads, seq_len);
+  float* dq_acc = reinterpret_cast<float*>(acc_base);
+  uint16_t* aux = reinterpret_cast<uint16_t*>(acc_base + align_up(64 * sizeof(float) * (size_t)batch * heads * padded));
   return launch_attention_bwd(q, k, v, o, d_o, lse, batch, heads, seq_len, head_dim, scale, *plan, dq,
-                              dk, dv, stats, dq_acc, static_cast<cudaStream_t>(stream));
+                              dk, dv, stats, dq_acc, aux, static_cast<cudaStream_t>(stream));
 }
 
 int rt_device_status(int32_t reset) {

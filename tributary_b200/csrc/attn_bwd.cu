@@ -20,6 +20,7 @@ namespace rt {
 namespace bwd {
 
 constexpr int kThreads = 576;         // producer, MMA, 16 softmax warps
+constexpr int kThreadsFused = 608;    // fused kernel: the same plus one dQ reduce warp
 constexpr int kSoftmaxThreads = 512;  // four per TMEM lane quadrant, each owning 32 of a row's 128 columns
 constexpr int kTmemCols = 512;
 
@@ -41,15 +42,21 @@ struct Cfg {
   // 512 TMEM columns per CTA: ask for enough shared memory that a second CTA
   // never lands on the same SM (it would only block in tcgen05.alloc).
   static constexpr int kDynSmem = (kSmemBytes + 1024) > 118 * 1024 ? (kSmemBytes + 1024) : 118 * 1024;
-  // fused dK/dV/dQ kernel: a dS^T tile [2 panels][128 keys][64 queries] bf16 after the stats ring
-  static constexpr int kDS = (kSmemBytes + 1023) & ~1023;
+  // Fused dK/dV/dQ kernel. After the Q / dO ring: a ring of row-statistic
+  // operand tiles [128 queries][16 bf16] (32-byte swizzle), then two constant
+  // tiles of the same shape (ones in columns 0-1, resp. 2-3), then the dS^T
+  // tile [2 panels][128 keys][64 queries] bf16 (128-byte swizzle), then one
+  // dQ staging slot [32 rows][16 fp32] (64-byte swizzle) per draining warp.
+  static constexpr int kAuxTileBytes = RT_TILE * 32;
+  static constexpr int kFAux = kR1 + kStages * kTileBytes;
+  static constexpr int kFOnes = kFAux + kStages * kAuxTileBytes;
+  static constexpr int kDS = kFOnes + 2 * kAuxTileBytes;
   static constexpr int kDSPanel = RT_TILE * 128;
-  // then the dQ staging tile: DH / 32 boxes of [128 rows][32 fp32] with the 128-byte swizzle
   static constexpr int kStg = kDS + 2 * kDSPanel;
-  static constexpr int kStgBox = RT_TILE * 128;
-  static constexpr int kStgBytes = (DH / 32) * kStgBox;
-  static constexpr int kDynSmemFused =
-      (kStg + kStgBytes + 1024) > 118 * 1024 ? (kStg + kStgBytes + 1024) : 118 * 1024;
+  static constexpr int kStgSlot = 32 * 16 * 4;
+  static constexpr int kStgBytes = (DH / 16) * 4 * kStgSlot;
+  static constexpr int kDynSmemFused = kStg + kStgBytes + 1024;
+  static_assert(kFAux % 1024 == 0 && kDS % 1024 == 0 && kStg % 1024 == 0, "fused layout alignment");
 };
 
 constexpr int kMaxTiles = 65536 / RT_TILE;
@@ -64,8 +71,8 @@ struct __align__(8) Barriers {
   uint64_t pb_full;        // softmax phase B done: dS (or dS^T) written
   uint64_t done;           // last gradient MMA complete
   uint64_t dq_ready;       // fused kernel: dQ partial of the tile in TMEM
-  uint64_t stg_full;       // fused kernel: dQ staging tile written (softmax warps)
-  uint64_t stg_free;       // fused kernel: previous TMA reduce has read the staging tile
+  uint64_t stg_full;       // fused kernel: dQ partial staged and fenced (one arrival per softmax warp)
+  uint64_t stg_free;       // fused kernel: the reduce warp's TMA has read the staged partial
   uint64_t drain;
 };
 
@@ -193,12 +200,15 @@ struct EpiSlice {
 // negated so they enter the exponent / difference as FMA addends:
 //   stats[bh][0][q] = -lse[bh][q] * log2(e)                 (0 for q >= S)
 //   stats[bh][1][q] = -sum_d dO[bh][q][d] * O[bh][q][d]     (0 for q >= S)
+// and, when aux is given, the fused kernel's operand row per padded query:
+//   aux[bh * Sp + q] = bf16 (a_hi, a_lo, d_hi, d_lo, 0 x 12),
+//   a = -lse / scale, d = stats[bh][1][q], x_hi = bf16(x), x_lo = bf16(x - x_hi).
 template <int DH>
 __global__ void __launch_bounds__(256) row_stats_kernel(const uint16_t* __restrict__ o,
                                                         const uint16_t* __restrict__ d_o,
                                                         const float* __restrict__ lse,
-                                                        float* __restrict__ stats, int S, int Sp,
-                                                        long long rows_padded) {
+                                                        float* __restrict__ stats, uint16_t* __restrict__ aux,
+                                                        float inv_scale, int S, int Sp, long long rows_padded) {
   constexpr int kLanesPerRow = DH / 8;
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long prow = gid / kLanesPerRow;
@@ -224,9 +234,18 @@ __global__ void __launch_bounds__(256) row_stats_kernel(const uint16_t* __restri
 #pragma unroll
   for (int off = kLanesPerRow / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, off);
   if (prow < rows_padded && sub == 0) {
+    const float l = in ? lse[bh * S + q] : 0.f;
     float* st = stats + bh * 2 * Sp;
-    st[q] = in ? -lse[bh * S + q] * 1.4426950408889634f : 0.f;
+    st[q] = in ? -l * 1.4426950408889634f : 0.f;
     st[Sp + q] = -acc;
+    if (aux != nullptr) {
+      const float a = -l * inv_scale, d = -acc;
+      const float a_hi = __bfloat162float(__float2bfloat16_rn(a));
+      const float d_hi = __bfloat162float(__float2bfloat16_rn(d));
+      uint4* dst = reinterpret_cast<uint4*>(aux + prow * 16);
+      dst[0] = make_uint4(pack_bf16x2(a_hi, a - a_hi), pack_bf16x2(d_hi, d - d_hi), 0u, 0u);
+      dst[1] = make_uint4(0u, 0u, 0u, 0u);
+    }
   }
 }
 
@@ -613,26 +632,79 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 // Fused dK, dV and dQ: one CTA per (b, h, k-tile), dkdv_kernel's pipeline plus
 // dQ, so S, dP and P are computed once per live tile instead of twice.
+//
+// Row statistics ride in the MMAs. row_stats_kernel writes per query q an
+// operand row aux[q] = (a_hi, a_lo, d_hi, d_lo, 0, ...) in bf16 with
+// a = -lse[q] / scale and d = -delta[q], each split into two bf16 parts whose
+// sum is exact to 2^-16 relative. One extra 16-deep k-step per product
+// multiplies it by a constant tile of ones (columns 0-1 for S, 2-3 for dP), so
+// TMEM receives S'^T = K Q^T + a and dP'^T = V dO^T - delta directly: then
+//   p = exp2(scale * log2(e) * S'^T)        dS = P o dP'^T
+// and the softmax warps read nothing but TMEM (warp-uniform per-column
+// statistics from shared memory cost four wavefronts per 16-byte load and
+// competed with the tensor core's operand reads for shared-memory bandwidth).
+//
 // Phase B writes dS^T (bf16) to a shared-memory tile [2 panels][128 keys][64
 // queries] with the 128-byte swizzle instead of TMEM. The MMAs read it twice:
 // as dS^T, K-major (dK += dS^T Q_i), and as dS, MN-major over both panels
 // (dQ_i = dS K, M = the 128 queries). dQ_i lands over columns [0, DH) of the
 // S^T buffer that dV_i has just consumed. Before arriving on phase A of the
-// next tile the softmax warps copy it into a shared staging tile (the 128-byte
-// swizzle, conflict-free), and the first softmax thread reduce-adds the tile
-// into the fp32 accumulator dq_acc [B*H][S padded][DH] with TMA
-// (cp.reduce.async.bulk.tensor, whole 128-byte lines); dq_convert_kernel
-// scales and rounds it afterwards. Every dQ row block gets one partial per
+// next tile each softmax warp copies its 32 rows x 16 columns of it into the
+// staging tile (DH / 16 boxes of [128 rows][16 fp32], 64-byte swizzle,
+// conflict-free); the proxy fence that phase B issues for the dS^T tile
+// covers these stores too, after which the warp arrives on stg_full. A
+// dedicated warp waits for all sixteen and reduce-adds the boxes into the fp32
+// accumulator dq_acc [B*H][S padded][DH] with TMA
+// (cp.reduce.async.bulk.tensor), then releases the staging tile (stg_free)
+// once the copies have read it: neither the fence nor the TMA issue, which
+// queues behind the other reduces, sits on the softmax warps' path.
+// dq_convert_kernel scales and rounds dq_acc afterwards. Every dQ row block gets one partial per
 // live key tile in an order the memory system decides, so dQ is reproducible
 // to fp32 rounding; dK and dV are written once.
 // TMEM as dkdv_kernel: S^T0 [0,128), S^T1 [128,256), dP^T [256,384), dV, dK.
 // ---------------------------------------------------------------------------
+
+// Phase A with the statistics already in the accumulator: p = exp2(c * s').
+__device__ __forceinline__ void softmax_phase_a_aux(uint32_t taddr, bool full, uint32_t mw, float c,
+                                                    uint32_t (&pk)[16]) {
+  uint32_t r[32];
+  tmem_ld32(taddr, r);
+  tmem_wait_ld();
+  if (!full) {
+#pragma unroll
+    for (int e = 0; e < 32; ++e) r[e] = ((mw >> e) & 1u) ? r[e] : __float_as_uint(-INFINITY);
+  }
+  const float2 c2 = make_float2(c, c);
+#pragma unroll
+  for (int e = 0; e < 32; e += 4) {
+    const float2 x01 = fmul2(make_float2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), c2);
+    const float2 x23 = fmul2(make_float2(__uint_as_float(r[e + 2]), __uint_as_float(r[e + 3])), c2);
+    pk[e >> 1] = pack_bf16x2(fast_exp2(x01.x), fast_exp2(x01.y));
+    pk[(e >> 1) + 1] = pack_bf16x2(fast_exp2(x23.x), fast_exp2(x23.y));
+  }
+}
+
+// Phase B with delta already subtracted: dS = P o dP'.
+__device__ __forceinline__ void softmax_phase_b_aux(uint32_t taddr, const uint32_t (&pk)[16], uint32_t (&ds)[16]) {
+  uint32_t d[32];
+  tmem_ld32(taddr, d);
+  tmem_wait_ld();
+#pragma unroll
+  for (int e = 0; e < 32; e += 4) {
+    const float2 g01 = fmul2(unpack_bf16x2(pk[e >> 1]), make_float2(__uint_as_float(d[e]), __uint_as_float(d[e + 1])));
+    const float2 g23 =
+        fmul2(unpack_bf16x2(pk[(e >> 1) + 1]), make_float2(__uint_as_float(d[e + 2]), __uint_as_float(d[e + 3])));
+    ds[e >> 1] = pack_bf16x2(g01.x, g01.y);
+    ds[(e >> 1) + 1] = pack_bf16x2(g23.x, g23.y);
+  }
+}
+
 template <int DH>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreadsFused, 1)
     dkdvq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                const rt_tile_plan plan, int H, int S, float scale, float scale_log2,
-                const float* __restrict__ stats, uint16_t* __restrict__ dk, uint16_t* __restrict__ dv,
+                const __grid_constant__ CUtensorMap tm_aux, const rt_tile_plan plan, int H, int S, float scale,
+                float scale_log2, uint16_t* __restrict__ dk, uint16_t* __restrict__ dv,
                 const __grid_constant__ CUtensorMap tm_acc) {
   using C = Cfg<DH>;
   constexpr int kST0 = 0, kDPT = 256, kDV = 384, kDK = 384 + DH;
@@ -650,7 +722,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int list_begin = plan.k2q_ptr[col_list];
   const int n_tiles = plan.k2q_ptr[col_list + 1] - list_begin;
   const int Sp = T * RT_TILE;
-  for (int i = threadIdx.x; i < n_tiles; i += kThreads) s_list[i] = plan.k2q_idx[list_begin + i];
+  for (int i = threadIdx.x; i < n_tiles; i += kThreadsFused) s_list[i] = plan.k2q_idx[list_begin + i];
+  // Constant ones tiles [2][128 rows][16 bf16], 32-byte swizzle (the 16-byte
+  // half j of row r sits at half j ^ ((r >> 2) & 1)): tile 0 has 1.0 in
+  // columns 0-1, tile 1 in columns 2-3. 512 threads write 16 bytes each.
+  if (threadIdx.x < 2 * C::kAuxTileBytes / 16) {
+    const int off = threadIdx.x * 16;
+    const int tile = off / C::kAuxTileBytes, row = (off % C::kAuxTileBytes) / 32, half = (off % 32) / 16;
+    const bool logical0 = (half ^ ((row >> 2) & 1)) == 0;
+    const uint32_t ones = 0x3F803F80u;  // two bf16 1.0
+    uint4 val = make_uint4(0u, 0u, 0u, 0u);
+    if (logical0) {
+      if (tile == 0) val.x = ones;
+      else val.y = ones;
+    }
+    *reinterpret_cast<uint4*>(smem + C::kFOnes + off) = val;
+    fence_proxy_async_smem();
+  }
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -675,13 +763,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = i % C::kStages;
         if (i >= C::kStages && !mbar_wait(&bars.ring_empty[s], ((i / C::kStages) - 1) & 1, &abort_flag)) break;
         const int qtile = s_list[i] & 0x7FFFFFFF;
-        mbar_arrive_expect_tx(&bars.ring_full[s], 2 * C::kTileBytes + C::kRowStatBytes);
+        mbar_arrive_expect_tx(&bars.ring_full[s], 2 * C::kTileBytes + C::kAuxTileBytes);
         tma_load_3d(smem + C::kR0 + s * C::kTileBytes, &tm_q, &bars.ring_full[s], 0, qtile * RT_TILE, bh);
         tma_load_3d(smem + C::kR1 + s * C::kTileBytes, &tm_do, &bars.ring_full[s], 0, qtile * RT_TILE, bh);
-        uint8_t* st = smem + C::kRL + s * C::kRowStatBytes;
-        const float* src = stats + (size_t)bh * 2 * Sp + (size_t)qtile * RT_TILE;
-        bulk_load(st, src, RT_TILE * 4, &bars.ring_full[s]);
-        bulk_load(st + RT_TILE * 4, src + Sp, RT_TILE * 4, &bars.ring_full[s]);
+        tma_load_2d(smem + C::kFAux + s * C::kAuxTileBytes, &tm_aux, &bars.ring_full[s], 0,
+                    bh * Sp + qtile * RT_TILE);
       }
       volatile int no_abort = 0;
       for (int ii = max(0, i - C::kStages); ii < i; ++ii)
@@ -696,20 +782,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t ds_addr = smem_u32(smem + C::kDS);
       const uint32_t k_addr = smem_u32(smem + C::kA0);
       const uint32_t v_addr = smem_u32(smem + C::kA1);
+      const uint64_t ones_s = sdesc(smem_u32(smem + C::kFOnes), 16, 256, SW_32B);
+      const uint64_t ones_dp = sdesc(smem_u32(smem + C::kFOnes + C::kAuxTileBytes), 16, 256, SW_32B);
       auto q_addr = [&](int i) { return smem_u32(smem + C::kR0 + (i % C::kStages) * C::kTileBytes); };
       auto do_addr = [&](int i) { return smem_u32(smem + C::kR1 + (i % C::kStages) * C::kTileBytes); };
-      auto issue_st = [&](int i) {  // S^T[i%2] = K Q_i^T
+      auto aux_desc = [&](int i) {
+        return sdesc(smem_u32(smem + C::kFAux + (i % C::kStages) * C::kAuxTileBytes), 16, 256, SW_32B);
+      };
+      auto issue_st = [&](int i) {  // S'^T[i%2] = K Q_i^T + a
 #pragma unroll
         for (int ks = 0; ks < DH / 16; ++ks)
           mma_ss(tmem + kST0 + (i & 1) * 128, sdesc(k_addr + ks * 32, 16, C::kSBO, C::kSwizzle),
                  sdesc(q_addr(i) + ks * 32, 16, C::kSBO, C::kSwizzle), idesc_s, ks > 0 ? 1u : 0u);
+        mma_ss(tmem + kST0 + (i & 1) * 128, ones_s, aux_desc(i), idesc_s, 1u);
         mma_commit(&bars.st_full[i & 1]);
       };
-      auto issue_dpt = [&](int i) {  // dP^T = V dO_i^T
+      auto issue_dpt = [&](int i) {  // dP'^T = V dO_i^T - delta
 #pragma unroll
         for (int ks = 0; ks < DH / 16; ++ks)
           mma_ss(tmem + kDPT, sdesc(v_addr + ks * 32, 16, C::kSBO, C::kSwizzle),
                  sdesc(do_addr(i) + ks * 32, 16, C::kSBO, C::kSwizzle), idesc_s, ks > 0 ? 1u : 0u);
+        mma_ss(tmem + kDPT, ones_dp, aux_desc(i), idesc_s, 1u);
         mma_commit(&bars.dp_full);
       };
       bool ok = mbar_wait(&bars.res_full, 0, &abort_flag) && mbar_wait(&bars.ring_full[0], 0, &abort_flag);
@@ -760,6 +853,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       volatile int no_abort = 0;
       mbar_wait(&bars.drain, 0, &no_abort);
     }
+  } else if (warp == 2 + kSoftmaxThreads / 32) {
+    // ---------------- dQ reduce warp ----------------
+    if (lane == 0 && n_tiles > 0) {
+      int t = 0;
+      for (; t < n_tiles; ++t) {
+        if (!mbar_wait(&bars.stg_full, t & 1, &abort_flag)) break;
+        const int row0 = bh * Sp + (s_list[t] & 0x7FFFFFFF) * RT_TILE;
+#pragma unroll
+        for (int g = 0; g < DH / 16; ++g)
+          tma_reduce_add_2d(&tm_acc, smem + C::kStg + g * 4 * C::kStgSlot, g * 16, row0);
+        bulk_commit_group();
+        bulk_wait_read_all();
+        mbar_arrive(&bars.stg_free);
+      }
+      bulk_wait_all();  // every reduce issued has completed
+    }
   } else {
     const int quad = warp & 3;
     const int grp = (warp - 2) >> 2;  // column group: queries [32 grp, 32 grp + 32) of every tile
@@ -772,47 +881,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       return ent >= 0 ? __ldg(masks_t + ((size_t)(ent & 0x7FFFFFFF) * RT_TILE + row) * 4) : 0xFFFFFFFFu;
     };
     // dQ partial of tile t (queries of q-tile s_list[t] in TMEM lanes = rows):
-    // this warp copies columns [16 grp, 16 grp + 16) of its 32 rows into the
-    // staging tile; the first softmax thread then reduce-adds the whole tile
-    // into dq_acc (TMA), and, before the next drain rewrites the tile, waits
-    // for that reduce to have read it.
-    const bool leader_warp = warp == 2;
-    auto drain_dq = [&](int t) -> bool {
+    // this warp owns rows [32 quad, 32 quad + 32) x columns [16 grp, 16 grp +
+    // 16) (grp < DH / 16): rows 32 quad + lane of box grp of the staging tile,
+    // 16-byte chunk c at chunk c ^ ((row >> 1) & 3), the 64-byte swizzle. The
+    // stores wait until the reduce warp's copy of the previous partial has
+    // read the tile; the caller fences them and arrives on stg_full.
+    const bool drains = grp * 16 < DH;
+    uint8_t* srow = smem + C::kStg + (drains ? (grp * 4 + quad) : 0) * C::kStgSlot + lane * 64;
+    auto stage_dq = [&](int t) -> bool {
       if (!mbar_wait_warp(&bars.dq_ready, t & 1, &abort_flag)) return false;
       tc_fence_after();
-      const bool has = grp * 16 < DH;
-      uint32_t r[16];
-      if (has) {
+      if (drains) {
+        uint32_t r[16];
         tmem_ld16(lane_base + kST0 + (t & 1) * 128 + grp * 16, r);
         tmem_wait_ld();
-      }
-      if (t > 0) {
-        if (leader_warp && lane == 0) {
-          bulk_wait_read_all();
-          mbar_arrive(&bars.stg_free);
-        }
-        if (!mbar_wait_warp(&bars.stg_free, (t - 1) & 1, &abort_flag)) return false;
-      }
-      if (has) {
-        uint8_t* box = smem + C::kStg + (grp >> 1) * C::kStgBox + row * 128;
+        if (t > 0 && !mbar_wait_warp(&bars.stg_free, (t - 1) & 1, &abort_flag)) return false;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int chunk = (grp & 1) * 4 + c;
-          *reinterpret_cast<uint4*>(box + ((chunk ^ (row & 7)) << 4)) =
+        for (int c = 0; c < 4; ++c)
+          *reinterpret_cast<uint4*>(srow + ((c ^ ((lane >> 1) & 3)) << 4)) =
               make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
-        }
-      }
-      fence_proxy_async_smem();
-      mbar_arrive_warp(&bars.stg_full);
-      if (leader_warp) {
-        if (!mbar_wait_warp(&bars.stg_full, t & 1, &abort_flag)) return false;
-        if (lane == 0) {
-          const int row0 = bh * Sp + (s_list[t] & 0x7FFFFFFF) * RT_TILE;
-#pragma unroll
-          for (int x = 0; x < DH / 32; ++x) tma_reduce_add_2d(&tm_acc, smem + C::kStg + x * C::kStgBox, x * 32, row0);
-          bulk_commit_group();
-        }
-        __syncwarp();
       }
       return true;
     };
@@ -822,24 +909,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool full = s_list[i] < 0;
       const uint32_t mk = mk_next;
       if (i + 1 < n_tiles) mk_next = load_mask(s_list[i + 1]);
-      const int stage = i % C::kStages;
-      if (!(ok = mbar_wait_warp(&bars.ring_full[stage], (i / C::kStages) & 1, &abort_flag))) break;
-      const float* nl = reinterpret_cast<const float*>(smem + C::kRL + stage * C::kRowStatBytes) + col0;
-      const float* nd = nl + RT_TILE;
       if (!(ok = mbar_wait_warp(&bars.st_full[i & 1], (i >> 1) & 1, &abort_flag))) break;
       tc_fence_after();
       uint32_t pk[16];
       const uint32_t st_addr = lane_base + kST0 + (i & 1) * 128 + col0;
-      softmax_phase_a<true>(st_addr, full, mk, scale_log2, nl, 0.f, pk);
+      softmax_phase_a_aux(st_addr, full, mk, scale_log2, pk);
       tmem_st16(st_addr, pk);  // P^T over the first 16 columns of this slice
       tmem_wait_st();
-      if (i > 0 && !(ok = drain_dq(i - 1))) break;
+      if (i > 0 && !(ok = stage_dq(i - 1))) break;
       tc_fence_before();
       mbar_arrive_warp(&bars.pa_full);
       if (!(ok = mbar_wait_warp(&bars.dp_full, i & 1, &abort_flag))) break;
       tc_fence_after();
       uint32_t ds[16];
-      softmax_phase_b_ds<true>(lane_base + kDPT + col0, pk, nd, 0.f, ds);
+      softmax_phase_b_aux(lane_base + kDPT + col0, pk, ds);
       // dS^T row `row`, queries [32 grp, 32 grp + 32): panel grp / 2, 16-byte
       // chunks (grp % 2) * 4 + c of the row, stored at chunk ^ (row % 8)
       uint8_t* drow = smem + C::kDS + (grp >> 1) * C::kDSPanel + row * 128;
@@ -849,12 +932,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         *reinterpret_cast<uint4*>(drow + ((chunk ^ (row & 7)) << 4)) =
             make_uint4(ds[4 * c], ds[4 * c + 1], ds[4 * c + 2], ds[4 * c + 3]);
       }
-      fence_proxy_async_smem();  // the tensor core reads the tile through the async proxy
+      fence_proxy_async_smem();  // the tensor core (dS^T) and the reduce warp's TMA (dQ_{i-1}) read through the async proxy
       tc_fence_before();
       mbar_arrive_warp(&bars.pb_full);
+      if (i > 0) mbar_arrive_warp(&bars.stg_full);
     }
-    if (ok && n_tiles > 0) ok = drain_dq(n_tiles - 1);
-    if (leader_warp && lane == 0) bulk_wait_all();  // every reduce issued has completed
+    if (ok && n_tiles > 0 && (ok = stage_dq(n_tiles - 1))) {
+      fence_proxy_async_smem();
+      mbar_arrive_warp(&bars.stg_full);
+    }
     if (ok && n_tiles > 0 && mbar_wait_warp(&bars.done, 0, &abort_flag)) {
       tc_fence_after();
       uint16_t* dst_v = dv + ((size_t)bh * S + key) * DH;
@@ -904,7 +990,7 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(const float* __restrict
 template <int DH>
 int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* o, const uint16_t* d_o,
            const float* lse, int B, int H, int S, float scale, const rt_tile_plan& plan, uint16_t* dq,
-           uint16_t* dk, uint16_t* dv, float* stats, float* dq_acc, cudaStream_t stream) {
+           uint16_t* dk, uint16_t* dv, float* stats, float* dq_acc, uint16_t* aux, cudaStream_t stream) {
   using C = Cfg<DH>;
   CUtensorMap tq, tk, tv, tdo;
   if (make_qkv_tensor_map(&tq, q, B * H, S, DH) != RT_OK || make_qkv_tensor_map(&tk, k, B * H, S, DH) != RT_OK ||
@@ -925,18 +1011,21 @@ int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16
   const int Sp = plan.tiles * RT_TILE;
   const long long rows_padded = (long long)B * H * Sp;
   const long long threads = rows_padded * (DH / 8);
-  row_stats_kernel<DH><<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(o, d_o, lse, stats, S, Sp,
-                                                                              rows_padded);
+  // fused path: the statistics ride in the MMAs as -lse / scale, so scale > 0
+  const bool fused = dq_acc != nullptr && aux != nullptr && scale > 0.f && scale < 3.0e38f;
+  row_stats_kernel<DH><<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
+      o, d_o, lse, stats, fused ? aux : nullptr, fused ? 1.0f / scale : 0.f, S, Sp, rows_padded);
   if (int st = check_launch("row_stats_kernel launch")) return st;
   const float scale_log2 = scale * 1.4426950408889634f;
   dim3 grid(plan.tiles, H, B);
-  if (dq_acc != nullptr) {  // fused: one pass for dK, dV and dQ
+  if (fused) {  // one pass for dK, dV and dQ
     cudaError_t e = cudaMemsetAsync(dq_acc, 0, sizeof(float) * (size_t)rows_padded * DH, stream);
     if (e != cudaSuccess) return cuda_failure(e, "cudaMemsetAsync(dq accumulator)");
-    CUtensorMap tacc;
+    CUtensorMap tacc, taux;
     if (make_acc_tensor_map(&tacc, dq_acc, rows_padded, DH) != RT_OK) return RT_ERR_CUDA;
-    dkdvq_kernel<DH><<<grid, kThreads, C::kDynSmemFused, stream>>>(tq, tk, tv, tdo, plan, H, S, scale, scale_log2,
-                                                                   stats, dk, dv, tacc);
+    if (make_aux_tensor_map(&taux, aux, rows_padded) != RT_OK) return RT_ERR_CUDA;
+    dkdvq_kernel<DH><<<grid, kThreadsFused, C::kDynSmemFused, stream>>>(tq, tk, tv, tdo, taux, plan, H, S, scale,
+                                                                   scale_log2, dk, dv, tacc);
     if (int st = check_launch("dkdvq_kernel launch")) return st;
     const long long rows = (long long)B * H * S;
     const long long cthreads = rows * (DH / 8);
@@ -956,11 +1045,11 @@ int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16
 int launch_attention_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* o,
                          const uint16_t* d_o, const float* lse, int B, int H, int S, int Dh, float scale,
                          const rt_tile_plan& plan, uint16_t* dq, uint16_t* dk, uint16_t* dv, float* stats,
-                         float* dq_acc, cudaStream_t stream) {
+                         float* dq_acc, uint16_t* aux, cudaStream_t stream) {
   if (Dh == 64)
-    return bwd::launch<64>(q, k, v, o, d_o, lse, B, H, S, scale, plan, dq, dk, dv, stats, dq_acc, stream);
+    return bwd::launch<64>(q, k, v, o, d_o, lse, B, H, S, scale, plan, dq, dk, dv, stats, dq_acc, aux, stream);
   if (Dh == 32)
-    return bwd::launch<32>(q, k, v, o, d_o, lse, B, H, S, scale, plan, dq, dk, dv, stats, dq_acc, stream);
+    return bwd::launch<32>(q, k, v, o, d_o, lse, B, H, S, scale, plan, dq, dk, dv, stats, dq_acc, aux, stream);
   return RT_ERR_UNSUPPORTED;
 }
 

@@ -79,5 +79,5 @@ extern "C" int rt_attention_bwd_noalloc(const uint16_t* q, const uint16_t* k, co
   const int st = noalloc::scratch_address(&scratch);
   if (st != RT_OK) return st;
   return launch_attention_bwd(q, k, v, o, d_o, lse, batch, heads, seq_len, head_dim, scale, *plan, dq, dk, dv,
-                              scratch, nullptr, static_cast<cudaStream_t>(stream));
+                              scratch, nullptr, nullptr, static_cast<cudaStream_t>(stream));
 }

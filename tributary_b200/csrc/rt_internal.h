@@ -27,11 +27,12 @@ int launch_attention_fwd(const uint16_t* q, const uint16_t* k, const uint16_t* v
 int launch_attention_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* o,
                          const uint16_t* d_o, const float* lse, int B, int H, int S, int Dh,
                          float scale, const rt_tile_plan& plan, uint16_t* dq, uint16_t* dk,
-                         uint16_t* dv, float* stats, float* dq_acc, cudaStream_t stream);
+                         uint16_t* dv, float* stats, float* dq_acc, uint16_t* aux, cudaStream_t stream);
 
 // TMA descriptor for a [rows_total][Dh] bf16 matrix viewed as (Dh, S, B*H),
 // box (Dh, 128, 1), 128B swizzle for Dh = 64, 64B swizzle for Dh = 32.
 int make_qkv_tensor_map(CUtensorMap* map, const void* base, int BH, int S, int Dh);
 int make_acc_tensor_map(CUtensorMap* map, float* base, long long rows, int Dh);
+int make_aux_tensor_map(CUtensorMap* map, uint16_t* base, long long rows);
 
 }  // namespace rt
