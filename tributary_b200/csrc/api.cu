@@ -157,17 +157,17 @@ int make_qkv_tensor_map(CUtensorMap* map, const void* base, int BH, int S, int D
   return r == CUDA_SUCCESS ? RT_OK : driver_failure((int)r, "cuTensorMapEncodeTiled");
 }
 
-// fp32 accumulator [rows][Dh] as boxes of 128 rows x 16 floats (64 B rows,
-// the 64-byte swizzle), for the TMA reduce-adds of the fused backward.
+// fp32 accumulator [rows][Dh] as boxes of 32 rows x 32 floats (128 B rows,
+// the 128-byte swizzle), for the TMA reduce-adds of the fused backward.
 int make_acc_tensor_map(CUtensorMap* map, float* base, long long rows, int Dh) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return driver_failure(-1, "cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)");
   cuuint64_t dims[2] = {(cuuint64_t)Dh, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)Dh * 4};
-  cuuint32_t box[2] = {16, (cuuint32_t)RT_TILE};
+  cuuint32_t box[2] = {32, 32};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? RT_OK : driver_failure((int)r, "cuTensorMapEncodeTiled(dq accumulator)");
 }

@@ -20,7 +20,7 @@ namespace rt {
 namespace bwd {
 
 constexpr int kThreads = 576;         // producer, MMA, 16 softmax warps
-constexpr int kThreadsFused = 608;    // fused kernel: the same plus one dQ reduce warp
+constexpr int kThreadsFused = 704;    // fused kernel: the same plus four dQ reduce warps (one per TMEM lane quadrant)
 constexpr int kSoftmaxThreads = 512;  // four per TMEM lane quadrant, each owning 32 of a row's 128 columns
 constexpr int kTmemCols = 512;
 
@@ -46,15 +46,17 @@ struct Cfg {
   // operand tiles [128 queries][16 bf16] (32-byte swizzle), then two constant
   // tiles of the same shape (ones in columns 0-1, resp. 2-3), then the dS^T
   // tile [2 panels][128 keys][64 queries] bf16 (128-byte swizzle), then one
-  // dQ staging slot [32 rows][16 fp32] (64-byte swizzle) per draining warp.
+  // dQ staging slot per reduce warp: DH / 32 boxes [32 rows][32 fp32]
+  // (128-byte swizzle).
   static constexpr int kAuxTileBytes = RT_TILE * 32;
   static constexpr int kFAux = kR1 + kStages * kTileBytes;
   static constexpr int kFOnes = kFAux + kStages * kAuxTileBytes;
   static constexpr int kDS = kFOnes + 2 * kAuxTileBytes;
   static constexpr int kDSPanel = RT_TILE * 128;
   static constexpr int kStg = kDS + 2 * kDSPanel;
-  static constexpr int kStgSlot = 32 * 16 * 4;
-  static constexpr int kStgBytes = (DH / 16) * 4 * kStgSlot;
+  static constexpr int kStgBox = 32 * 32 * 4;
+  static constexpr int kStgSlot = (DH / 32) * kStgBox;
+  static constexpr int kStgBytes = 4 * kStgSlot;
   static constexpr int kDynSmemFused = kStg + kStgBytes + 1024;
   static_assert(kFAux % 1024 == 0 && kDS % 1024 == 0 && kStg % 1024 == 0, "fused layout alignment");
 };
@@ -71,8 +73,7 @@ struct __align__(8) Barriers {
   uint64_t pb_full;        // softmax phase B done: dS (or dS^T) written
   uint64_t done;           // last gradient MMA complete
   uint64_t dq_ready;       // fused kernel: dQ partial of the tile in TMEM
-  uint64_t stg_full;       // fused kernel: dQ partial staged and fenced (one arrival per softmax warp)
-  uint64_t stg_free;       // fused kernel: the reduce warp's TMA has read the staged partial
+  uint64_t dq_drained;     // fused kernel: the reduce warps have read the dQ partial out of TMEM
   uint64_t drain;
 };
 
@@ -89,8 +90,7 @@ __device__ __forceinline__ void init_barriers(Barriers& bars, int stages) {
   mbar_init(&bars.pb_full, kSoftmaxThreads / 32);
   mbar_init(&bars.done, 1);
   mbar_init(&bars.dq_ready, 1);
-  mbar_init(&bars.stg_full, kSoftmaxThreads / 32);
-  mbar_init(&bars.stg_free, 1);
+  mbar_init(&bars.dq_drained, 4);
   mbar_init(&bars.drain, 1);
   fence_mbar_init();
 }
@@ -648,16 +648,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 // queries] with the 128-byte swizzle instead of TMEM. The MMAs read it twice:
 // as dS^T, K-major (dK += dS^T Q_i), and as dS, MN-major over both panels
 // (dQ_i = dS K, M = the 128 queries). dQ_i lands over columns [0, DH) of the
-// S^T buffer that dV_i has just consumed. Before arriving on phase A of the
-// next tile each softmax warp copies its 32 rows x 16 columns of it into the
-// staging tile (DH / 16 boxes of [128 rows][16 fp32], 64-byte swizzle,
-// conflict-free); the proxy fence that phase B issues for the dS^T tile
-// covers these stores too, after which the warp arrives on stg_full. A
-// dedicated warp waits for all sixteen and reduce-adds the boxes into the fp32
-// accumulator dq_acc [B*H][S padded][DH] with TMA
-// (cp.reduce.async.bulk.tensor), then releases the staging tile (stg_free)
-// once the copies have read it: neither the fence nor the TMA issue, which
-// queues behind the other reduces, sits on the softmax warps' path.
+// S^T buffer that dV_i has just consumed. Four reduce warps, one per TMEM lane
+// quadrant, copy it out (32 queries x DH each), arrive on dq_drained -- the
+// MMA issuer waits for that before S^T_{i+2} reuses the buffer -- and then
+// stage it in shared memory (128-byte swizzle, conflict-free) and reduce-add
+// it into the fp32 accumulator dq_acc [B*H][S padded][DH] with TMA
+// (cp.reduce.async.bulk.tensor), each warp on its own slot and bulk group.
+// The softmax warps never touch dQ.
 // dq_convert_kernel scales and rounds dq_acc afterwards. Every dQ row block gets one partial per
 // live key tile in an order the memory system decides, so dQ is reproducible
 // to fp32 rounding; dK and dV are written once.
@@ -823,6 +820,8 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
         if (i + 1 < n_tiles) {
           if (!(ok = mbar_wait(&bars.ring_full[(i + 1) % C::kStages], ((i + 1) / C::kStages) & 1, &abort_flag)))
             break;
+          // the buffer S^T_{i+1} lands in holds dQ_{i-1} until the reduce warps have read it
+          if (i > 0 && !(ok = mbar_wait(&bars.dq_drained, (i - 1) & 1, &abort_flag))) break;
           tc_fence_after();
           issue_st(i + 1);
         }
@@ -853,22 +852,44 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
       volatile int no_abort = 0;
       mbar_wait(&bars.drain, 0, &no_abort);
     }
-  } else if (warp == 2 + kSoftmaxThreads / 32) {
-    // ---------------- dQ reduce warp ----------------
-    if (lane == 0 && n_tiles > 0) {
-      int t = 0;
-      for (; t < n_tiles; ++t) {
-        if (!mbar_wait(&bars.stg_full, t & 1, &abort_flag)) break;
-        const int row0 = bh * Sp + (s_list[t] & 0x7FFFFFFF) * RT_TILE;
+  } else if (warp >= 2 + kSoftmaxThreads / 32) {
+    // ---------------- dQ reduce warps ----------------
+    // Warp w reads TMEM lanes [32 (w % 4), +32): queries 32 quad + lane of the
+    // tile, all DH columns. Its slot holds DH / 32 boxes [32 rows][32 fp32],
+    // 16-byte chunk c of row r at chunk c ^ (r % 8) (the 128-byte swizzle).
+    const int quad = warp & 3;
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+    uint8_t* slot = smem + C::kStg + (warp - 2 - kSoftmaxThreads / 32) * C::kStgSlot;
+    for (int t = 0; t < n_tiles; ++t) {
+      if (!mbar_wait_warp(&bars.dq_ready, t & 1, &abort_flag)) break;
+      tc_fence_after();
+      uint32_t r[DH];
 #pragma unroll
-        for (int g = 0; g < DH / 16; ++g)
-          tma_reduce_add_2d(&tm_acc, smem + C::kStg + g * 4 * C::kStgSlot, g * 16, row0);
-        bulk_commit_group();
-        bulk_wait_read_all();
-        mbar_arrive(&bars.stg_free);
+      for (int x = 0; x < DH / 32; ++x)
+        tmem_ld32(lane_base + kST0 + (t & 1) * 128 + x * 32, *reinterpret_cast<uint32_t(*)[32]>(r + x * 32));
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive_warp(&bars.dq_drained);
+      if (lane == 0) bulk_wait_read_all();  // this warp's previous reduces have read the slot
+      __syncwarp();
+#pragma unroll
+      for (int x = 0; x < DH / 32; ++x) {
+        uint8_t* srow = slot + x * C::kStgBox + lane * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(srow + ((c ^ (lane & 7)) << 4)) =
+              make_uint4(r[x * 32 + 4 * c], r[x * 32 + 4 * c + 1], r[x * 32 + 4 * c + 2], r[x * 32 + 4 * c + 3]);
       }
-      bulk_wait_all();  // every reduce issued has completed
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int row0 = bh * Sp + (s_list[t] & 0x7FFFFFFF) * RT_TILE + quad * 32;
+#pragma unroll
+        for (int x = 0; x < DH / 32; ++x) tma_reduce_add_2d(&tm_acc, slot + x * C::kStgBox, x * 32, row0);
+        bulk_commit_group();
+      }
     }
+    if (lane == 0) bulk_wait_all();  // every reduce this warp issued has completed
   } else {
     const int quad = warp & 3;
     const int grp = (warp - 2) >> 2;  // column group: queries [32 grp, 32 grp + 32) of every tile
@@ -879,29 +900,6 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
     const uint32_t* masks_t = plan.tile_masks_t + ((size_t)col_list * T) * RT_TILE * 4 + grp;
     auto load_mask = [&](int ent) {
       return ent >= 0 ? __ldg(masks_t + ((size_t)(ent & 0x7FFFFFFF) * RT_TILE + row) * 4) : 0xFFFFFFFFu;
-    };
-    // dQ partial of tile t (queries of q-tile s_list[t] in TMEM lanes = rows):
-    // this warp owns rows [32 quad, 32 quad + 32) x columns [16 grp, 16 grp +
-    // 16) (grp < DH / 16): rows 32 quad + lane of box grp of the staging tile,
-    // 16-byte chunk c at chunk c ^ ((row >> 1) & 3), the 64-byte swizzle. The
-    // stores wait until the reduce warp's copy of the previous partial has
-    // read the tile; the caller fences them and arrives on stg_full.
-    const bool drains = grp * 16 < DH;
-    uint8_t* srow = smem + C::kStg + (drains ? (grp * 4 + quad) : 0) * C::kStgSlot + lane * 64;
-    auto stage_dq = [&](int t) -> bool {
-      if (!mbar_wait_warp(&bars.dq_ready, t & 1, &abort_flag)) return false;
-      tc_fence_after();
-      if (drains) {
-        uint32_t r[16];
-        tmem_ld16(lane_base + kST0 + (t & 1) * 128 + grp * 16, r);
-        tmem_wait_ld();
-        if (t > 0 && !mbar_wait_warp(&bars.stg_free, (t - 1) & 1, &abort_flag)) return false;
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          *reinterpret_cast<uint4*>(srow + ((c ^ ((lane >> 1) & 3)) << 4)) =
-              make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
-      }
-      return true;
     };
     uint32_t mk_next = n_tiles > 0 ? load_mask(s_list[0]) : 0u;
     bool ok = true;
@@ -916,7 +914,6 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
       softmax_phase_a_aux(st_addr, full, mk, scale_log2, pk);
       tmem_st16(st_addr, pk);  // P^T over the first 16 columns of this slice
       tmem_wait_st();
-      if (i > 0 && !(ok = stage_dq(i - 1))) break;
       tc_fence_before();
       mbar_arrive_warp(&bars.pa_full);
       if (!(ok = mbar_wait_warp(&bars.dp_full, i & 1, &abort_flag))) break;
@@ -932,14 +929,9 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
         *reinterpret_cast<uint4*>(drow + ((chunk ^ (row & 7)) << 4)) =
             make_uint4(ds[4 * c], ds[4 * c + 1], ds[4 * c + 2], ds[4 * c + 3]);
       }
-      fence_proxy_async_smem();  // the tensor core (dS^T) and the reduce warp's TMA (dQ_{i-1}) read through the async proxy
+      fence_proxy_async_smem();  // the tensor core reads the tile through the async proxy
       tc_fence_before();
       mbar_arrive_warp(&bars.pb_full);
-      if (i > 0) mbar_arrive_warp(&bars.stg_full);
-    }
-    if (ok && n_tiles > 0 && (ok = stage_dq(n_tiles - 1))) {
-      fence_proxy_async_smem();
-      mbar_arrive_warp(&bars.stg_full);
     }
     if (ok && n_tiles > 0 && mbar_wait_warp(&bars.done, 0, &abort_flag)) {
       tc_fence_after();
