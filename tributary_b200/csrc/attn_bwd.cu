@@ -772,37 +772,51 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
       mbar_wait(&bars.res_full, 0, &no_abort);
     }
   } else if (warp == 1) {
-    if (lane == 0 && n_tiles > 0) {
+    // ---------------- MMA issue: the whole warp waits, one elected lane issues ----------------
+    if (n_tiles > 0) {
+      const bool leader = elect_one_sync();
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false, false);
       constexpr uint32_t idesc_g = idesc_bf16_f32(128, DH, false, true);
       constexpr uint32_t idesc_dq = idesc_bf16_f32(128, DH, true, true);
-      const uint32_t ds_addr = smem_u32(smem + C::kDS);
-      const uint32_t k_addr = smem_u32(smem + C::kA0);
-      const uint32_t v_addr = smem_u32(smem + C::kA1);
+      // descriptor start addresses advance in 16-byte units: +2 per 16-deep
+      // k-step along a K-major row, +kRowBytes per 16 rows of an MN-major tile
+      constexpr uint32_t kRowStep = C::kRowBytes;
+      const uint64_t k_kmaj = sdesc(smem_u32(smem + C::kA0), 16, C::kSBO, C::kSwizzle);
+      const uint64_t v_kmaj = sdesc(smem_u32(smem + C::kA1), 16, C::kSBO, C::kSwizzle);
+      const uint64_t k_mn = sdesc(smem_u32(smem + C::kA0), 0, C::kSBO, C::kSwizzle);
+      const uint64_t ds_mn = sdesc(smem_u32(smem + C::kDS), C::kDSPanel, 1024, SW_128B);
+      const uint64_t ds_kmaj = sdesc(smem_u32(smem + C::kDS), 16, 1024, SW_128B);
       const uint64_t ones_s = sdesc(smem_u32(smem + C::kFOnes), 16, 256, SW_32B);
       const uint64_t ones_dp = sdesc(smem_u32(smem + C::kFOnes + C::kAuxTileBytes), 16, 256, SW_32B);
-      auto q_addr = [&](int i) { return smem_u32(smem + C::kR0 + (i % C::kStages) * C::kTileBytes); };
-      auto do_addr = [&](int i) { return smem_u32(smem + C::kR1 + (i % C::kStages) * C::kTileBytes); };
+      auto ring_desc = [&](int base, int i, uint32_t lbo) {
+        return sdesc(smem_u32(smem + base + (i % C::kStages) * C::kTileBytes), lbo, C::kSBO, C::kSwizzle);
+      };
       auto aux_desc = [&](int i) {
         return sdesc(smem_u32(smem + C::kFAux + (i % C::kStages) * C::kAuxTileBytes), 16, 256, SW_32B);
       };
       auto issue_st = [&](int i) {  // S'^T[i%2] = K Q_i^T + a
+        const uint64_t qd = ring_desc(C::kR0, i, 16), ad = aux_desc(i);
+        const uint32_t d = tmem + kST0 + (i & 1) * 128;
+        if (leader) {
 #pragma unroll
-        for (int ks = 0; ks < DH / 16; ++ks)
-          mma_ss(tmem + kST0 + (i & 1) * 128, sdesc(k_addr + ks * 32, 16, C::kSBO, C::kSwizzle),
-                 sdesc(q_addr(i) + ks * 32, 16, C::kSBO, C::kSwizzle), idesc_s, ks > 0 ? 1u : 0u);
-        mma_ss(tmem + kST0 + (i & 1) * 128, ones_s, aux_desc(i), idesc_s, 1u);
-        mma_commit(&bars.st_full[i & 1]);
+          for (int ks = 0; ks < DH / 16; ++ks) mma_ss(d, k_kmaj + ks * 2, qd + ks * 2, idesc_s, ks > 0 ? 1u : 0u);
+          mma_ss(d, ones_s, ad, idesc_s, 1u);
+          mma_commit(&bars.st_full[i & 1]);
+        }
+        __syncwarp();
       };
       auto issue_dpt = [&](int i) {  // dP'^T = V dO_i^T - delta
+        const uint64_t dd = ring_desc(C::kR1, i, 16), ad = aux_desc(i);
+        if (leader) {
 #pragma unroll
-        for (int ks = 0; ks < DH / 16; ++ks)
-          mma_ss(tmem + kDPT, sdesc(v_addr + ks * 32, 16, C::kSBO, C::kSwizzle),
-                 sdesc(do_addr(i) + ks * 32, 16, C::kSBO, C::kSwizzle), idesc_s, ks > 0 ? 1u : 0u);
-        mma_ss(tmem + kDPT, ones_dp, aux_desc(i), idesc_s, 1u);
-        mma_commit(&bars.dp_full);
+          for (int ks = 0; ks < DH / 16; ++ks)
+            mma_ss(tmem + kDPT, v_kmaj + ks * 2, dd + ks * 2, idesc_s, ks > 0 ? 1u : 0u);
+          mma_ss(tmem + kDPT, ones_dp, ad, idesc_s, 1u);
+          mma_commit(&bars.dp_full);
+        }
+        __syncwarp();
       };
-      bool ok = mbar_wait(&bars.res_full, 0, &abort_flag) && mbar_wait(&bars.ring_full[0], 0, &abort_flag);
+      bool ok = mbar_wait_warp(&bars.res_full, 0, &abort_flag) && mbar_wait_warp(&bars.ring_full[0], 0, &abort_flag);
       tc_fence_after();
       if (ok) {
         issue_st(0);
@@ -811,46 +825,53 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
       // S^T_{i+1} is issued only once phase A of tile i has been observed, so
       // no barrier can run two phases ahead of its waiter.
       for (int i = 0; ok && i < n_tiles; ++i) {
-        if (!(ok = mbar_wait(&bars.pa_full, i & 1, &abort_flag))) break;
+        if (!(ok = mbar_wait_warp(&bars.pa_full, i & 1, &abort_flag))) break;
         tc_fence_after();
         // S^T_{i+1} first: the softmax warps start its phase A while dV_i
         // runs (MMA issue blocks for the MMA's duration, so issuing dV_i
         // first would put it on the softmax's critical path). S^T_{i+1}
         // targets the other buffer; dV_i reads P^T_i from this one.
         if (i + 1 < n_tiles) {
-          if (!(ok = mbar_wait(&bars.ring_full[(i + 1) % C::kStages], ((i + 1) / C::kStages) & 1, &abort_flag)))
+          if (!(ok = mbar_wait_warp(&bars.ring_full[(i + 1) % C::kStages], ((i + 1) / C::kStages) & 1, &abort_flag)))
             break;
           // the buffer S^T_{i+1} lands in holds dQ_{i-1} until the reduce warps have read it
-          if (i > 0 && !(ok = mbar_wait(&bars.dq_drained, (i - 1) & 1, &abort_flag))) break;
+          if (i > 0 && !(ok = mbar_wait_warp(&bars.dq_drained, (i - 1) & 1, &abort_flag))) break;
           tc_fence_after();
           issue_st(i + 1);
         }
+        const uint64_t dom = ring_desc(C::kR1, i, 0), qm = ring_desc(C::kR0, i, 0);
+        if (leader) {
 #pragma unroll
-        for (int ks = 0; ks < RT_TILE / 16; ++ks)  // dV += P^T_i dO_i
-          mma_ts(tmem + kDV, tmem + kST0 + (i & 1) * 128 + packed_col(ks),
-                 sdesc(do_addr(i) + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_g,
-                 (i > 0 || ks > 0) ? 1u : 0u);
-        if (!(ok = mbar_wait(&bars.pb_full, i & 1, &abort_flag))) break;
+          for (int ks = 0; ks < RT_TILE / 16; ++ks)  // dV += P^T_i dO_i
+            mma_ts(tmem + kDV, tmem + kST0 + (i & 1) * 128 + packed_col(ks), dom + ks * kRowStep, idesc_g,
+                   (i > 0 || ks > 0) ? 1u : 0u);
+        }
+        __syncwarp();
+        if (!(ok = mbar_wait_warp(&bars.pb_full, i & 1, &abort_flag))) break;
         tc_fence_after();
-        // dQ_i first: its drain precedes the softmax's next phase-A arrival,
-        // which the next S^T / dV wait for; dK_i is not waited on until the end
+        // dQ_i first: the reduce warps drain it while dK_i runs; dK_i is not
+        // waited on until the end
+        if (leader) {
 #pragma unroll
-        for (int ks = 0; ks < RT_TILE / 16; ++ks)  // dQ_i = dS K (A: the dS^T tile read MN-major over both panels)
-          mma_ss(tmem + kST0 + (i & 1) * 128, sdesc(ds_addr + ks * 16 * 128, C::kDSPanel, 1024, SW_128B),
-                 sdesc(k_addr + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_dq, ks > 0 ? 1u : 0u);
-        mma_commit(&bars.dq_ready);
+          for (int ks = 0; ks < RT_TILE / 16; ++ks)  // dQ_i = dS K (A: the dS^T tile read MN-major over both panels)
+            mma_ss(tmem + kST0 + (i & 1) * 128, ds_mn + ks * 128, k_mn + ks * kRowStep, idesc_dq, ks > 0 ? 1u : 0u);
+          mma_commit(&bars.dq_ready);
 #pragma unroll
-        for (int ks = 0; ks < RT_TILE / 16; ++ks)  // dK += dS^T_i Q_i (A: the same tile, K-major)
-          mma_ss(tmem + kDK, sdesc(ds_addr + (ks >> 2) * C::kDSPanel + (ks & 3) * 32, 16, 1024, SW_128B),
-                 sdesc(q_addr(i) + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_g,
-                 (i > 0 || ks > 0) ? 1u : 0u);
-        mma_commit(&bars.ring_empty[i % C::kStages]);
+          for (int ks = 0; ks < RT_TILE / 16; ++ks)  // dK += dS^T_i Q_i (A: the same tile, K-major)
+            mma_ss(tmem + kDK, ds_kmaj + (ks >> 2) * (C::kDSPanel / 16) + (ks & 3) * 2, qm + ks * kRowStep, idesc_g,
+                   (i > 0 || ks > 0) ? 1u : 0u);
+          mma_commit(&bars.ring_empty[i % C::kStages]);
+        }
+        __syncwarp();
         if (i + 1 < n_tiles) issue_dpt(i + 1);
       }
-      mma_commit(&bars.done);
-      mma_commit(&bars.drain);
+      if (leader) {
+        mma_commit(&bars.done);
+        mma_commit(&bars.drain);
+      }
+      __syncwarp();
       volatile int no_abort = 0;
-      mbar_wait(&bars.drain, 0, &no_abort);
+      mbar_wait_warp(&bars.drain, 0, &no_abort);
     }
   } else if (warp >= 2 + kSoftmaxThreads / 32) {
     // ---------------- dQ reduce warps ----------------

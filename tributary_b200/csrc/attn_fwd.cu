@@ -340,8 +340,9 @@ __global__ void __launch_bounds__(kMainThreads, 1)
       mbar_wait(&bars.kv_full[gg % kStages], (gg / kStages) & 1, &no_abort);
     for (int kk = max(0, kq - 2); kk < kq; ++kk) mbar_wait(&bars.q_full[kk & 1], (kk >> 1) & 1, &no_abort);
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // ---------------- MMA issuer: the whole warp waits, one elected lane issues ----------------
+    {
+      const bool leader = elect_one_sync();
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, DH, false, true);
       bool ok = true;
@@ -351,25 +352,28 @@ __global__ void __launch_bounds__(kMainThreads, 1)
       int nS_next = n_items > 1 ? item_ntiles(item_id(1)) : 0;
       auto issue_next_s = [&]() -> bool {  // issues S_gS, advances the cursor; false when done
         while (kS < n_items && tS >= nS) {  // leave finished (or empty) items, releasing their Q slot
-          if (nS == 0 && !(ok = mbar_wait(&bars.q_full[kS & 1], (kS >> 1) & 1, &abort_flag))) return false;
-          mma_commit(&bars.q_empty[kS & 1]);
+          if (nS == 0 && !(ok = mbar_wait_warp(&bars.q_full[kS & 1], (kS >> 1) & 1, &abort_flag))) return false;
+          if (leader) mma_commit(&bars.q_empty[kS & 1]);
+          __syncwarp();
           ++kS;
           tS = 0;
           nS = nS_next;
           nS_next = kS + 1 < n_items ? item_ntiles(item_id(kS + 1)) : 0;
         }
         if (kS >= n_items) return false;
-        if (tS == 0 && !(ok = mbar_wait(&bars.q_full[kS & 1], (kS >> 1) & 1, &abort_flag))) return false;
+        if (tS == 0 && !(ok = mbar_wait_warp(&bars.q_full[kS & 1], (kS >> 1) & 1, &abort_flag))) return false;
         const int st = gS % kStages;
-        if (!(ok = mbar_wait(&bars.kv_full[st], (gS / kStages) & 1, &abort_flag))) return false;
+        if (!(ok = mbar_wait_warp(&bars.kv_full[st], (gS / kStages) & 1, &abort_flag))) return false;
         tc_fence_after();
-        const uint32_t q_addr = smem_u32(smem + C::kQOff + (kS & 1) * C::kTileBytes);
-        const uint32_t k_addr = smem_u32(smem + C::kKOff + st * C::kTileBytes);
+        const uint64_t qd = sdesc(smem_u32(smem + C::kQOff + (kS & 1) * C::kTileBytes), 16, C::kSBO, C::kSwizzle);
+        const uint64_t kd = sdesc(smem_u32(smem + C::kKOff + st * C::kTileBytes), 16, C::kSBO, C::kSwizzle);
+        const uint32_t d = tmem + (gS % kSets) * 128;
+        if (leader) {
 #pragma unroll
-        for (int ks = 0; ks < DH / 16; ++ks)
-          mma_ss(tmem + (gS % kSets) * 128, sdesc(q_addr + ks * 32, 16, C::kSBO, C::kSwizzle),
-                 sdesc(k_addr + ks * 32, 16, C::kSBO, C::kSwizzle), idesc_s, ks > 0 ? 1u : 0u);
-        mma_commit(&bars.st_full[gS % kSets]);
+          for (int ks = 0; ks < DH / 16; ++ks) mma_ss(d, qd + ks * 2, kd + ks * 2, idesc_s, ks > 0 ? 1u : 0u);
+          mma_commit(&bars.st_full[gS % kSets]);
+        }
+        __syncwarp();
         ++tS;
         ++gS;
         return true;
@@ -383,27 +387,34 @@ __global__ void __launch_bounds__(kMainThreads, 1)
         const int n = nP_next;
         nP_next = kP + 1 < n_items ? item_ntiles(item_id(kP + 1)) : 0;
         const int ob = kP & 1;
-        if (kP >= 2 && !(ok = mbar_wait(&bars.o_free[ob], ((kP - 2) >> 1) & 1, &abort_flag))) break;
+        if (kP >= 2 && !(ok = mbar_wait_warp(&bars.o_free[ob], ((kP - 2) >> 1) & 1, &abort_flag))) break;
         for (int t = 0; ok && t < n; ++t, ++g) {
           const int set = g % kSets;
-          if (!(ok = mbar_wait(&bars.p_full[set], (g / kSets) & 1, &abort_flag))) break;
+          if (!(ok = mbar_wait_warp(&bars.p_full[set], (g / kSets) & 1, &abort_flag))) break;
           tc_fence_after();
-          const uint32_t v_addr = smem_u32(smem + C::kVOff + (g % kStages) * C::kTileBytes);
+          // V is MN-major: +kRowBytes (16-byte units) per 16 keys
+          const uint64_t vd = sdesc(smem_u32(smem + C::kVOff + (g % kStages) * C::kTileBytes), 0, C::kSBO, C::kSwizzle);
+          if (leader) {
 #pragma unroll
-          for (int ks = 0; ks < RT_TILE / 16; ++ks)  // O += P_g V_g
-            mma_ts(tmem + kOMain + ob * DH, tmem + set * 128 + ks * 8,
-                   sdesc(v_addr + ks * 16 * C::kRowBytes, 0, C::kSBO, C::kSwizzle), idesc_o,
-                   (t > 0 || ks > 0) ? 1u : 0u);
-          mma_commit(&bars.o_done[set]);
-          mma_commit(&bars.kv_empty[g % kStages]);
-          if (t == n - 1) mma_commit(&bars.item_done[ob]);
+            for (int ks = 0; ks < RT_TILE / 16; ++ks)  // O += P_g V_g
+              mma_ts(tmem + kOMain + ob * DH, tmem + set * 128 + ks * 8, vd + ks * C::kRowBytes, idesc_o,
+                     (t > 0 || ks > 0) ? 1u : 0u);
+            mma_commit(&bars.o_done[set]);
+            mma_commit(&bars.kv_empty[g % kStages]);
+            if (t == n - 1) mma_commit(&bars.item_done[ob]);
+          }
+          __syncwarp();
           issue_next_s();  // into the S buffer P_g just left
         }
-        if (n == 0) mma_commit(&bars.item_done[ob]);
+        if (n == 0) {
+          if (leader) mma_commit(&bars.item_done[ob]);
+          __syncwarp();
+        }
       }
-      mma_commit(&bars.drain);
+      if (leader) mma_commit(&bars.drain);
+      __syncwarp();
       volatile int no_abort = 0;
-      mbar_wait(&bars.drain, 0, &no_abort);
+      mbar_wait_warp(&bars.drain, 0, &no_abort);
     }
   } else if (warp < 2 + kEpiWarps) {
     // ---------------- epilogue warpgroup ----------------

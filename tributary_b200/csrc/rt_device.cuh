@@ -311,6 +311,17 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo_bytes, ui
   return d;
 }
 
+// One lane of the (fully active) warp: the issuer of a batch of tcgen05.mma.
+// Running the issuing loop on the whole warp keeps descriptors and loop state
+// warp-uniform (uniform datapath) instead of in one divergent lane, so the
+// tensor core is not left waiting on issue slots the other warps of the
+// sub-partition compete for.
+__device__ __forceinline__ bool elect_one_sync() {
+  uint32_t pred = 0;
+  asm volatile("{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}" : "=r"(pred));
+  return pred != 0;
+}
+
 // D[tmem] (+)= A[smem] * B[smem]
 __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                        uint32_t accumulate) {
