@@ -528,7 +528,8 @@ __global__ void __launch_bounds__(kMainThreads, 1)
             for (int a = 0; a < 2; ++a) {
               const float2 x =
                   ffma2(make_float2(__uint_as_float(r[e + 2 * a]), __uint_as_float(r[e + 2 * a + 1])), c2, nm2);
-              const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+              // half of the exponentials on the MUFU, half on the FMA pipe
+              const float2 p = a == 0 ? make_float2(fast_exp2(x.x), fast_exp2(x.y)) : exp2_poly2(x);
               lsum[a] = fadd2(lsum[a], p);
               pk[(e >> 1) + a] = pack_bf16x2(p.x, p.y);
             }
