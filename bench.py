@@ -49,6 +49,13 @@ CONFIGS = {
 
 FLOPS_PER_LIVE_TILE = {"fwd": 4, "bwd": 10}  # x 128^2 x Dh per live (b, h, tile pair)
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one dkdvq_kernel
+# launch -- the fused dK/dV/dQ backward, the dominant kernel -- from an ncu
+# capture of this workload (summarised under profiles/); about the same for
+# every mask kind: q, k, v, dO and the row statistics read once, dK and dV
+# written once, plus the fp32 dQ accumulator's L2 misses under the reduce-adds.
+NCU_DKDVQ_TRAFFIC = {"rt_attn_fwd_bwd_b8_s4096_h16_d64": 647.2e6}
+
 
 def measured_peaks():
     path = os.path.join(REPO, "MEASURED_PEAKS.json")
@@ -407,6 +414,8 @@ def run_our_arm(args, cfg):
     peak_tf, peak_gbs, peak_src = measured_peaks()
     attn_ms = part_ms["fwd"] + part_ms["bwd"]
     achieved_tf = (flops["fwd"] + flops["bwd"]) / (attn_ms * 1e-3) / 1e12
+    bwd_tf = flops["bwd"] / (part_ms["bwd"] * 1e-3) / 1e12
+    fwd_tf = flops["fwd"] / (part_ms["fwd"] * 1e-3) / 1e12
     densities = {KIND_NAMES[i]: wl.nnz[i] / (cfgd["B"] * wl.tiles * wl.tiles) for i in range(4)}
     if rank == 0:
         line = {
@@ -426,10 +435,18 @@ def run_our_arm(args, cfg):
             "frac_of_bf16_peak": achieved_tf / peak_tf,
             "breakdown_ms_per_step": part_ms,
             "breakdown_ms_by_kind": kind_ms,
-            "roofline": {"bound": "tensor", "kernel": "attention fwd+bwd (attn_fwd, row_stats, dkdv, dq)",
-                         "achieved": achieved_tf, "peak": peak_tf, "unit": "TFLOP/s",
-                         "frac": achieved_tf / peak_tf, "peak_source": peak_src + " bf16 dense (burst)",
-                         "traffic": None},
+            # dominant kernel: dkdvq_kernel, timed with CUDA events around each
+            # rt_attention_bwd call (its row_stats and dq_convert launches are 7%
+            # of that time); per-launch flops over the average launch time
+            "roofline": {"bound": "tensor",
+                         "kernel": "dkdvq_kernel (fused dK/dV/dQ backward), timed as rt_attention_bwd",
+                         "achieved": bwd_tf, "peak": peak_tf, "unit": "TFLOP/s",
+                         "frac": bwd_tf / peak_tf, "peak_source": peak_src + " bf16 dense (burst)",
+                         "traffic": NCU_DKDVQ_TRAFFIC.get(cfgd["name"]),
+                         "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
+                         "algorithmic_flops_per_launch": flops["bwd"] / 4,
+                         "forward": {"kernel": "attn_fwd_kernel", "achieved": fwd_tf, "frac": fwd_tf / peak_tf},
+                         "fwd_plus_bwd": {"achieved": achieved_tf, "frac": achieved_tf / peak_tf}},
             "e2e": {"value": world * cells_step / (e2e_ms * 1e-3), "unit": "cells/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": wl.launches_per_step() * args.steps,
