@@ -838,6 +838,11 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
           if (i > 0 && !(ok = mbar_wait_warp(&bars.dq_drained, (i - 1) & 1, &abort_flag))) break;
           tc_fence_after();
           issue_st(i + 1);
+        } else if (i > 0 && !(ok = mbar_wait_warp(&bars.dq_drained, (i - 1) & 1, &abort_flag))) {
+          // last tile: no S^T_{i+1} waits for the reduce warps, but dQ_i must not complete
+          // dq_ready's next phase before every reduce warp has taken the previous one
+          // (a waiter two phases behind would read the parity wrongly and never return)
+          break;
         }
         const uint64_t dom = ring_desc(C::kR1, i, 0), qm = ring_desc(C::kR0, i, 0);
         if (leader) {
