@@ -107,3 +107,30 @@ def test_entry_points_work_from_a_worker_thread(cuda_lib):
     t.join()
     assert "e" not in out, out.get("e")
     _same_up_to_dq_order(ref, out["r"])
+
+
+def test_backward_repeated_under_concurrent_copies(cuda_lib):
+    """The fused backward's dQ reduce warps run behind the MMA issuer by up to a
+    tile; every barrier phase must still be taken by each of its waiters before
+    the next one completes. Repeat dense many-tile calls while a large copy runs
+    on another stream (which shifts the timing) and require a clean device
+    status and identical dK / dV every time."""
+    import torch
+    from tributary_b200.attention import attention_bwd, attention_fwd, device_status
+    c = Case((56, 2, 2048, 3, 4, 8, 0.7, 0.0), 3, h=4, dh=64, seed=11)
+    o, lse = attention_fwd(c.qd, c.kd, c.vd, c.plan, c.scale)
+    ref = attention_bwd(c.qd, c.kd, c.vd, o, lse, c.dod, c.plan, c.scale)
+    assert device_status() == 0
+    side = torch.cuda.Stream()
+    src = torch.empty(64 << 20, dtype=torch.uint8, device="cuda")
+    host = torch.empty(64 << 20, dtype=torch.uint8).pin_memory()
+    for it in range(12):
+        with torch.cuda.stream(side):
+            if it % 2:
+                host.copy_(src, non_blocking=True)
+            else:
+                src.copy_(host, non_blocking=True)
+        dq, dk, dv = attention_bwd(c.qd, c.kd, c.vd, o, lse, c.dod, c.plan, c.scale)
+        torch.cuda.synchronize()
+        assert device_status() == 0, it
+        assert torch.equal(dk, ref[1]) and torch.equal(dv, ref[2]), it
