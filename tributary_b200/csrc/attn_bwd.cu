@@ -70,6 +70,7 @@ struct __align__(8) Barriers {
   uint64_t st_full[2];     // S (or S^T) buffer b computed
   uint64_t dp_full;        // dP (or dP^T) computed
   uint64_t pa_full;        // softmax phase A done: S buffer read (and P^T written)
+  uint64_t pa_full_odd;    // fused kernel: phase A of odd tiles (pa_full takes the even ones)
   uint64_t pb_full;        // softmax phase B done: dS (or dS^T) written
   uint64_t done;           // last gradient MMA complete
   uint64_t dq_ready;       // fused kernel: dQ partial of the tile in TMEM
@@ -87,6 +88,7 @@ __device__ __forceinline__ void init_barriers(Barriers& bars, int stages) {
   mbar_init(&bars.st_full[1], 1);
   mbar_init(&bars.dp_full, 1);
   mbar_init(&bars.pa_full, kSoftmaxThreads / 32);  // one arrival per softmax warp
+  mbar_init(&bars.pa_full_odd, kSoftmaxThreads / 32);
   mbar_init(&bars.pb_full, kSoftmaxThreads / 32);
   mbar_init(&bars.done, 1);
   mbar_init(&bars.dq_ready, 1);
@@ -816,34 +818,26 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
         }
         __syncwarp();
       };
+      // S'^T runs two tiles ahead: S'^T_{i+2} is issued as soon as its buffer
+      // (i % 2) is free -- dV_i has read P^T_i from it (in-order pipe) and the
+      // reduce warps have drained dQ_i -- instead of after phase A of tile
+      // i + 1, so the softmax finds every S'^T waiting for it. Phase A
+      // arrives on pa_full / pa_full_odd by tile parity: with S'^T_{i+1}
+      // already issued, the softmax can finish phase A of tile i + 1 before
+      // this warp has waited for tile i.
       bool ok = mbar_wait_warp(&bars.res_full, 0, &abort_flag) && mbar_wait_warp(&bars.ring_full[0], 0, &abort_flag);
       tc_fence_after();
       if (ok) {
         issue_st(0);
         issue_dpt(0);
-      }
-      // S^T_{i+1} is issued only once phase A of tile i has been observed, so
-      // no barrier can run two phases ahead of its waiter.
-      for (int i = 0; ok && i < n_tiles; ++i) {
-        if (!(ok = mbar_wait_warp(&bars.pa_full, i & 1, &abort_flag))) break;
-        tc_fence_after();
-        // S^T_{i+1} first: the softmax warps start its phase A while dV_i
-        // runs (MMA issue blocks for the MMA's duration, so issuing dV_i
-        // first would put it on the softmax's critical path). S^T_{i+1}
-        // targets the other buffer; dV_i reads P^T_i from this one.
-        if (i + 1 < n_tiles) {
-          if (!(ok = mbar_wait_warp(&bars.ring_full[(i + 1) % C::kStages], ((i + 1) / C::kStages) & 1, &abort_flag)))
-            break;
-          // the buffer S^T_{i+1} lands in holds dQ_{i-1} until the reduce warps have read it
-          if (i > 0 && !(ok = mbar_wait_warp(&bars.dq_drained, (i - 1) & 1, &abort_flag))) break;
+        if (n_tiles > 1 && (ok = mbar_wait_warp(&bars.ring_full[1], 0, &abort_flag))) {
           tc_fence_after();
-          issue_st(i + 1);
-        } else if (i > 0 && !(ok = mbar_wait_warp(&bars.dq_drained, (i - 1) & 1, &abort_flag))) {
-          // last tile: no S^T_{i+1} waits for the reduce warps, but dQ_i must not complete
-          // dq_ready's next phase before every reduce warp has taken the previous one
-          // (a waiter two phases behind would read the parity wrongly and never return)
-          break;
+          issue_st(1);
         }
+      }
+      for (int i = 0; ok && i < n_tiles; ++i) {
+        if (!(ok = mbar_wait_warp((i & 1) ? &bars.pa_full_odd : &bars.pa_full, (i >> 1) & 1, &abort_flag))) break;
+        tc_fence_after();
         const uint64_t dom = ring_desc(C::kR1, i, 0), qm = ring_desc(C::kR0, i, 0);
         if (leader) {
 #pragma unroll
@@ -854,8 +848,6 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
         __syncwarp();
         if (!(ok = mbar_wait_warp(&bars.pb_full, i & 1, &abort_flag))) break;
         tc_fence_after();
-        // dQ_i first: the reduce warps drain it while dK_i runs; dK_i is not
-        // waited on until the end
         if (leader) {
 #pragma unroll
           for (int ks = 0; ks < RT_TILE / 16; ++ks)  // dQ_i = dS K (A: the dS^T tile read MN-major over both panels)
@@ -868,7 +860,19 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
           mma_commit(&bars.ring_empty[i % C::kStages]);
         }
         __syncwarp();
-        if (i + 1 < n_tiles) issue_dpt(i + 1);
+        if (i + 1 < n_tiles) {
+          issue_dpt(i + 1);  // its ring stage was waited for when S'^T_{i+1} was issued
+          // dQ_i out of buffer i % 2 before S'^T_{i+2} lands there; this wait also
+          // keeps dQ_{i+1} from completing dq_ready's next phase before every
+          // reduce warp has taken this one
+          if (!(ok = mbar_wait_warp(&bars.dq_drained, i & 1, &abort_flag))) break;
+          if (i + 2 < n_tiles) {
+            if (!(ok = mbar_wait_warp(&bars.ring_full[(i + 2) % C::kStages], ((i + 2) / C::kStages) & 1, &abort_flag)))
+              break;
+            tc_fence_after();
+            issue_st(i + 2);
+          }
+        }
       }
       if (leader) {
         mma_commit(&bars.done);
@@ -941,7 +945,7 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
       tmem_st16(st_addr, pk);  // P^T over the first 16 columns of this slice
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive_warp(&bars.pa_full);
+      mbar_arrive_warp((i & 1) ? &bars.pa_full_odd : &bars.pa_full);
       if (!(ok = mbar_wait_warp(&bars.dp_full, i & 1, &abort_flag))) break;
       tc_fence_after();
       uint32_t ds[16];
