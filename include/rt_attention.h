@@ -76,7 +76,7 @@ typedef struct rt_tile_plan {
   uint32_t* tile_masks;    /* [batch][T][T][128][4]  element bits, query-major (partial tiles) */
   uint32_t* tile_masks_t;  /* [batch][T][T][128][4]  element bits, key-major   (partial tiles) */
   uint32_t* fk_bits;       /* [batch][max_rows][ceil(max_rows/32)]  packed adjacency (scratch) */
-  int32_t* nnz;            /* [1] number of live tiles over the batch                         */
+  int32_t* nnz;            /* [1 + batch] number of live tiles over the batch, then scratch    */
 } rt_tile_plan;
 
 /* Bytes of device memory a tile plan needs. */

@@ -96,9 +96,11 @@ def mask_for_kind(kind, seq_row_ids, fk_adj, column_ids, is_padding):
 
 
 def permute_mask(mask, perm):
-    """mask_perm[b,i,j] = mask[b, perm[b,i], perm[b,j]]  (layers.py:144-152)."""
+    """mask_perm[b,i,j] = mask[b, perm[b,i], perm[b,j]]  (layers.py:144-152);
+    indices past the end clamp to S-1, as jax gathers do."""
     perm = np.asarray(perm).astype(np.int64)
     b, s = perm.shape
+    perm = np.minimum(perm, s - 1)
     bidx = np.arange(b)[:, None, None]
     return mask[bidx, perm[:, :, None], perm[:, None, :]]
 

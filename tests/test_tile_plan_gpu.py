@@ -33,9 +33,10 @@ def to_dev(bt):
     return out
 
 
-def check_plan(bt, kind, dev_bt):
+def check_plan(bt, kind, dev_bt, perm=None):
     from tributary_b200.attention import build_tile_plan
-    perm = orc.perm_for_kind(bt, kind)
+    if perm is None:
+        perm = orc.perm_for_kind(bt, kind)
     import torch
     perm_d = torch.from_numpy(np.ascontiguousarray(perm).view(np.int16)).cuda()
     plan = build_tile_plan(perm_d, dev_bt["seq_row_ids"], dev_bt["column_ids"],
@@ -107,3 +108,17 @@ def test_row_ids_beyond_R_are_clamped(cuda_lib):
         n = plan.nnz()
         assert p2.nnz() == n
         assert torch.equal(p2.q2k()[1][:n], plan.q2k()[1][:n])
+
+
+def test_orders_that_are_not_permutations(cuda_lib):
+    """An order with repeated and out-of-range entries (clamped to S-1) is not a
+    permutation: p_i == p_j then holds off the diagonal, and the prepass must
+    still match the oracle's gather of the mask (the per-key diagonal path)."""
+    bt = orc.make_batch(39, 2, 384, 3, 2, 6, 0.8, 0.1)
+    dev_bt = to_dev(bt)
+    for kind in range(4):
+        perm = np.array(orc.perm_for_kind(bt, kind), dtype=np.uint16, copy=True)
+        perm[0, 5:9] = perm[0, 200]          # repeats inside sample 0
+        perm[0, 300:303] = 65535             # past the end: clamps to S-1
+        perm[1, 17] = perm[1, 18]            # one repeat in sample 1
+        check_plan(bt, kind, dev_bt, perm=perm)

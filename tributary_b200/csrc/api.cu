@@ -53,7 +53,7 @@ PlanLayout plan_layout(int B, int S, int R) {
   L.masks = take(sizeof(uint32_t) * 4 * RT_TILE * B * T * T);
   L.masks_t = take(sizeof(uint32_t) * 4 * RT_TILE * B * T * T);
   L.fk = take(sizeof(uint32_t) * B * (size_t)R * WR);
-  L.nnz = take(sizeof(int32_t));
+  L.nnz = take(sizeof(int32_t) * (1 + (size_t)B));  // the count, then per-sample perm flags
   L.total = off;
   return L;
 }

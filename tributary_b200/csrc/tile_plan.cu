@@ -44,47 +44,66 @@ __global__ void fk_pack_kernel(const uint8_t* __restrict__ fk_adj, int R, int WR
   }
 }
 
-// One CTA per (b, q-tile, k-tile), one query row per thread; KIND is a
-// template parameter so the element loop carries no per-element branch on it.
-// The warp walks the keys in lockstep, and in the sampler's row orders the
-// keys of a tile come in runs of one row, so the fk word a key needs is
-// cached per thread and reloaded only when the row's word changes.
-template <int KIND>
+// flags[b] = 1 when min(perm[b][.], S-1) is a permutation of [0, S): then
+// p_i == p_j only for i == j, and the diagonal term of the element rule is
+// the identity. One CTA per sample marks each value in a shared bitmap.
+__global__ void __launch_bounds__(1024) perm_check_kernel(const uint16_t* __restrict__ perm, int S,
+                                                           int32_t* __restrict__ flags) {
+  __shared__ uint32_t bm[65536 / 32];
+  __shared__ int dup;
+  const int b = blockIdx.x;
+  const int words = (S + 31) / 32;
+  for (int w = threadIdx.x; w < words; w += blockDim.x) bm[w] = 0u;
+  if (threadIdx.x == 0) dup = 0;
+  __syncthreads();
+  for (int x = threadIdx.x; x < S; x += blockDim.x) {
+    const int p = min((int)perm[(size_t)b * S + x], S - 1);
+    const uint32_t bit = 1u << (p & 31);
+    if (atomicOr(&bm[p >> 5], bit) & bit) dup = 1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) flags[b] = dup ? 0 : 1;
+}
+
+constexpr int kKeyTilesPerCta = 8;
+constexpr int kMaxStagedWords = 64;
+
+// One CTA per (b, q-tile, run of kKeyTilesPerCta key tiles); thread = query
+// row. For each key tile the keys are grouped inside each warp by the value
+// the relation compares -- row id (feature, neighbor) or column id (column) --
+// with __match_any_sync, giving per warp a table of (value, 32-bit key set).
+// In the sampler's cell orders a tile holds runs of one row or column, so a
+// table has a handful of entries, and a query evaluates its 128 key bits as
+// the OR of the key sets whose value its relation admits (one test per
+// group instead of one per key), ANDed with the keys' validity. The feature /
+// neighbor relation tests bit `value` of the query row's packed fk row, staged
+// in shared memory once per CTA (odd row stride: conflict-free) when it has at
+// most kMaxStagedWords words. The diagonal term p_i == p_j is i == j for
+// samples whose perm is a permutation (flags from perm_check_kernel) and is
+// tested key by key otherwise.
+template <int KIND, bool kStaged>
 __global__ void __launch_bounds__(128) tile_mask_kernel(
     const uint16_t* __restrict__ perm, const uint16_t* __restrict__ seq_row_ids,
     const int32_t* __restrict__ column_ids, const uint8_t* __restrict__ is_padding,
     const uint32_t* __restrict__ fk_bits, int S, int R, int WR, rt_tile_plan plan) {
-  const int kt = blockIdx.x;
+  constexpr bool kFk = KIND == RT_MASK_FEATURE || KIND == RT_MASK_NEIGHBOR;
   const int qt = blockIdx.y;
   const int b = blockIdx.z;
   const int T = plan.tiles;
+  const int kt_begin = blockIdx.x * kKeyTilesPerCta;
+  const int kt_end = min(T, kt_begin + kKeyTilesPerCta);
   const int t = threadIdx.x;
   const int lane = t & 31;
   const int warp = t >> 5;
 
   __shared__ int s_korig[RT_TILE];
-  __shared__ int s_krow[RT_TILE];
-  __shared__ int s_kcol[RT_TILE];
-  __shared__ unsigned char s_kpad[RT_TILE];
+  __shared__ uint32_t s_valid[4];
+  __shared__ int s_gkey[4][32];
+  __shared__ uint32_t s_gbits[4][32];
+  __shared__ int s_gcount[4];
+  extern __shared__ uint32_t s_fk[];  // [128][WR | 1] when kStaged
 
   const size_t boff = (size_t)b * S;
-  {
-    const int j = kt * RT_TILE + t;
-    if (j < S) {
-      const int pj = min((int)perm[boff + j], S - 1);  // out-of-range perm entries clamp
-      int rj = seq_row_ids[boff + pj];
-      if (R > 0 && rj > R - 1) rj = R - 1;
-      s_korig[t] = pj;
-      s_krow[t] = rj;
-      s_kcol[t] = column_ids[boff + pj];
-      s_kpad[t] = is_padding[boff + pj] != 0;
-    } else {
-      s_korig[t] = -1;
-      s_krow[t] = 0;
-      s_kcol[t] = 0;
-      s_kpad[t] = 1;
-    }
-  }
   const int i = qt * RT_TILE + t;
   const bool qin = i < S;
   int pi = -2, ri = 0, ci = 0;
@@ -96,75 +115,106 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
     ci = column_ids[boff + pi];
     padi = is_padding[boff + pi] != 0;
   }
-  const uint32_t* fkrow = (R > 0 && fk_bits != nullptr) ? fk_bits + ((size_t)b * R + ri) * WR : nullptr;
-  __syncthreads();
+  const bool perm_ok = plan.nnz[1 + b] != 0;
+  const uint32_t* fkrow = (kFk && R > 0 && fk_bits != nullptr) ? fk_bits + ((size_t)b * R + ri) * WR : nullptr;
+  const int fk_stride = WR | 1;
+  if (kStaged && fkrow != nullptr)
+    for (int w = 0; w < WR; ++w) s_fk[t * fk_stride + w] = __ldg(fkrow + w);
+  auto fk_bit = [&](int r) -> bool {
+    if (fkrow == nullptr) return false;
+    const uint32_t word = kStaged ? s_fk[t * fk_stride + (r >> 5)] : __ldg(fkrow + (r >> 5));
+    return (word >> (r & 31)) & 1u;
+  };
 
-  uint32_t w4[4];
-  int cached_w = -1;  // fk word index held in cached_bits (warp-uniform: all lanes see the same key)
-  uint32_t cached_bits = 0;
-#pragma unroll
-  for (int w = 0; w < 4; ++w) {
-    uint32_t word = 0;
-    if (qin) {
-#pragma unroll 8
-      for (int u = 0; u < 32; ++u) {
-        const int j = w * 32 + u;
-        const int pj = s_korig[j];
-        bool m = false;
-        if (pj >= 0) {
-          const bool valid = !padi && !s_kpad[j];
-          bool rel;
-          if (KIND == RT_MASK_COLUMN) {
-            rel = ci == s_kcol[j];
-          } else if (KIND == RT_MASK_FEATURE || KIND == RT_MASK_NEIGHBOR) {
-            const int rj = s_krow[j];
-            uint32_t fk = 0u;
-            if (fkrow != nullptr) {
-              if ((rj >> 5) != cached_w) {
-                cached_w = rj >> 5;
-                cached_bits = __ldg(fkrow + cached_w);
-              }
-              fk = (cached_bits >> (rj & 31)) & 1u;
-            }
-            rel = (KIND == RT_MASK_FEATURE && ri == rj) || fk != 0u;
-          } else {
-            rel = true;
-          }
-          m = (rel && valid) || (pi == pj);
+  for (int kt = kt_begin; kt < kt_end; ++kt) {
+    {  // key metadata: validity bits, diagonal candidates and the warp's group table
+      const int j = kt * RT_TILE + t;
+      const bool jin = j < S;
+      int pj = -1, rj = 0, cj = 0;
+      bool padj = true;
+      if (jin) {
+        pj = min((int)perm[boff + j], S - 1);  // out-of-range perm entries clamp
+        rj = seq_row_ids[boff + pj];
+        if (R > 0 && rj > R - 1) rj = R - 1;
+        cj = column_ids[boff + pj];
+        padj = is_padding[boff + pj] != 0;
+      }
+      s_korig[t] = pj;
+      const uint32_t vb = __ballot_sync(0xFFFFFFFFu, jin && !padj);
+      if (lane == 0) s_valid[warp] = vb;
+      if (KIND != RT_MASK_FULL) {
+        const int gk = KIND == RT_MASK_COLUMN ? cj : rj;
+        const uint32_t same = __match_any_sync(0xFFFFFFFFu, gk);
+        const bool leader = (__ffs(same) - 1) == lane;
+        const uint32_t lb = __ballot_sync(0xFFFFFFFFu, leader);
+        if (leader) {
+          const int g = __popc(lb & ((1u << lane) - 1u));
+          s_gkey[warp][g] = gk;
+          s_gbits[warp][g] = same;
         }
-        word |= (m ? 1u : 0u) << u;
+        if (lane == 0) s_gcount[warp] = __popc(lb);
       }
     }
-    w4[w] = word;
-  }
+    __syncthreads();
 
-  const int any = __syncthreads_or((w4[0] | w4[1] | w4[2] | w4[3]) != 0u);
-  const int all = __syncthreads_and(qin && (w4[0] & w4[1] & w4[2] & w4[3]) == 0xFFFFFFFFu);
-  if (!any) return;  // block-uniform
-  const size_t tile_q = ((size_t)b * T + qt) * T + kt;
-  const size_t tile_k = ((size_t)b * T + kt) * T + qt;
-  if (t == 0) {
-    const size_t wi = ((size_t)b * T + qt) * plan.words + (kt >> 5);
-    atomicOr(plan.live_bits + wi, 1u << (kt & 31));
-    if (all) atomicOr(plan.full_bits + wi, 1u << (kt & 31));
-  }
-  if (all) return;  // block-uniform
-  reinterpret_cast<uint4*>(plan.tile_masks)[tile_q * RT_TILE + t] =
-      make_uint4(w4[0], w4[1], w4[2], w4[3]);
-  // Transpose 128x128 bits: for key j, this warp's 32 queries form word `warp`
-  // of key j's row in the key-major copy.
-  uint32_t tw[4] = {0u, 0u, 0u, 0u};
+    uint32_t w4[4] = {0u, 0u, 0u, 0u};
+    if (qin && !padi) {
 #pragma unroll
-  for (int w = 0; w < 4; ++w) {
-#pragma unroll 8
-    for (int u = 0; u < 32; ++u) {
-      const uint32_t bal = __ballot_sync(0xFFFFFFFFu, (w4[w] >> u) & 1u);
-      if (lane == u) tw[w] = bal;
+      for (int w = 0; w < 4; ++w) {
+        uint32_t rel = 0u;
+        if (KIND == RT_MASK_FULL) {
+          rel = 0xFFFFFFFFu;
+        } else {
+          const int n = s_gcount[w];
+          for (int g = 0; g < n; ++g) {
+            const int key = s_gkey[w][g];
+            bool r;
+            if (KIND == RT_MASK_COLUMN) r = ci == key;
+            else if (KIND == RT_MASK_FEATURE) r = ri == key || fk_bit(key);
+            else r = fk_bit(key);
+            if (r) rel |= s_gbits[w][g];
+          }
+        }
+        w4[w] = rel & s_valid[w];
+      }
     }
-  }
-  uint32_t* dst = plan.tile_masks_t + tile_k * RT_TILE * 4;
+    if (qin) {
+      if (perm_ok) {
+        if (kt == qt) w4[warp] |= 1u << lane;  // p_i == p_j exactly when i == j
+      } else {
+#pragma unroll 8
+        for (int u = 0; u < RT_TILE; ++u)
+          if (s_korig[u] == pi) w4[u >> 5] |= 1u << (u & 31);
+      }
+    }
+
+    const int any = __syncthreads_or((w4[0] | w4[1] | w4[2] | w4[3]) != 0u);
+    const int all = __syncthreads_and(qin && (w4[0] & w4[1] & w4[2] & w4[3]) == 0xFFFFFFFFu);
+    if (!any) continue;  // block-uniform; the barriers above end every read of this tile's tables
+    const size_t tile_q = ((size_t)b * T + qt) * T + kt;
+    const size_t tile_k = ((size_t)b * T + kt) * T + qt;
+    if (t == 0) {
+      const size_t wi = ((size_t)b * T + qt) * plan.words + (kt >> 5);
+      atomicOr(plan.live_bits + wi, 1u << (kt & 31));
+      if (all) atomicOr(plan.full_bits + wi, 1u << (kt & 31));
+    }
+    if (all) continue;  // block-uniform
+    reinterpret_cast<uint4*>(plan.tile_masks)[tile_q * RT_TILE + t] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+    // Transpose 128x128 bits: for key j, this warp's 32 queries form word `warp`
+    // of key j's row in the key-major copy.
+    uint32_t tw[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-  for (int w = 0; w < 4; ++w) dst[(size_t)(w * 32 + lane) * 4 + warp] = tw[w];
+    for (int w = 0; w < 4; ++w) {
+#pragma unroll 8
+      for (int u = 0; u < 32; ++u) {
+        const uint32_t bal = __ballot_sync(0xFFFFFFFFu, (w4[w] >> u) & 1u);
+        if (lane == u) tw[w] = bal;
+      }
+    }
+    uint32_t* dst = plan.tile_masks_t + tile_k * RT_TILE * 4;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) dst[(size_t)(w * 32 + lane) * 4 + warp] = tw[w];
+  }
 }
 
 // Single block: CSR lists (q2k over (b,qt) rows, k2q over (b,kt) rows) from the bitmaps.
@@ -261,19 +311,28 @@ int launch_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids, co
                                                   plan.fk_bits);
     fk_bits = plan.fk_bits;
   }
-  const dim3 grid(T, T, B);
+  perm_check_kernel<<<B, 1024, 0, stream>>>(perm, S, plan.nnz + 1);
+  const dim3 grid((T + kKeyTilesPerCta - 1) / kKeyTilesPerCta, T, B);
+  const bool staged = WR <= kMaxStagedWords;
+  const size_t fk_smem = sizeof(uint32_t) * RT_TILE * (size_t)(WR | 1);
   if (kind == RT_MASK_COLUMN)
-    tile_mask_kernel<RT_MASK_COLUMN><<<grid, RT_TILE, 0, stream>>>(perm, seq_row_ids, column_ids, is_padding,
-                                                                   fk_bits, S, R, WR, plan);
+    tile_mask_kernel<RT_MASK_COLUMN, false><<<grid, RT_TILE, 0, stream>>>(perm, seq_row_ids, column_ids,
+                                                                          is_padding, fk_bits, S, R, WR, plan);
+  else if (kind == RT_MASK_FEATURE && staged)
+    tile_mask_kernel<RT_MASK_FEATURE, true><<<grid, RT_TILE, fk_smem, stream>>>(perm, seq_row_ids, column_ids,
+                                                                                is_padding, fk_bits, S, R, WR, plan);
   else if (kind == RT_MASK_FEATURE)
-    tile_mask_kernel<RT_MASK_FEATURE><<<grid, RT_TILE, 0, stream>>>(perm, seq_row_ids, column_ids, is_padding,
-                                                                    fk_bits, S, R, WR, plan);
+    tile_mask_kernel<RT_MASK_FEATURE, false><<<grid, RT_TILE, 0, stream>>>(perm, seq_row_ids, column_ids,
+                                                                           is_padding, fk_bits, S, R, WR, plan);
+  else if (kind == RT_MASK_NEIGHBOR && staged)
+    tile_mask_kernel<RT_MASK_NEIGHBOR, true><<<grid, RT_TILE, fk_smem, stream>>>(perm, seq_row_ids, column_ids,
+                                                                                 is_padding, fk_bits, S, R, WR, plan);
   else if (kind == RT_MASK_NEIGHBOR)
-    tile_mask_kernel<RT_MASK_NEIGHBOR><<<grid, RT_TILE, 0, stream>>>(perm, seq_row_ids, column_ids, is_padding,
-                                                                     fk_bits, S, R, WR, plan);
+    tile_mask_kernel<RT_MASK_NEIGHBOR, false><<<grid, RT_TILE, 0, stream>>>(perm, seq_row_ids, column_ids,
+                                                                            is_padding, fk_bits, S, R, WR, plan);
   else
-    tile_mask_kernel<RT_MASK_FULL><<<grid, RT_TILE, 0, stream>>>(perm, seq_row_ids, column_ids, is_padding,
-                                                                 fk_bits, S, R, WR, plan);
+    tile_mask_kernel<RT_MASK_FULL, false><<<grid, RT_TILE, 0, stream>>>(perm, seq_row_ids, column_ids,
+                                                                        is_padding, fk_bits, S, R, WR, plan);
   tile_list_kernel<<<1, 1024, 0, stream>>>(plan);
   return check_launch("tile plan kernels launch");
 }
