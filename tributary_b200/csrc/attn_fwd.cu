@@ -150,7 +150,8 @@ constexpr int kSets = 3;
 constexpr int kSetWarps = 4;
 constexpr int kSoftmaxWarps = kSets * kSetWarps;
 constexpr int kEpiWarps = 4;
-constexpr int kMainThreads = 32 * (2 + kEpiWarps + kSoftmaxWarps);
+constexpr int kSIssueWarp = 2 + kEpiWarps + kSoftmaxWarps;  // issues the S MMAs; warp 1 issues PV
+constexpr int kMainThreads = 32 * (kSIssueWarp + 1);
 constexpr int kMainTmemCols = 512;
 constexpr int kOMain = kSets * 128;
 constexpr int kStages = 4;
@@ -179,10 +180,10 @@ struct MainCfg {
 struct __align__(8) MainBarriers {
   uint64_t q_full[2], q_empty[2];
   uint64_t kv_full[kStages], kv_empty[kStages];
-  uint64_t st_full[kSets], p_full[kSets], o_done[kSets];
+  uint64_t st_full[kSets], p_full[kSets], pv_done[kSets];
   uint64_t item_done[2], o_free[2];
   uint64_t sdiag_full[2], lsum_full[2];
-  uint64_t drain;
+  uint64_t drain, drain_s;
 };
 
 struct ItemCoord {
@@ -262,9 +263,10 @@ __global__ void __launch_bounds__(kMainThreads, 1)
     for (int i = 0; i < kSets; ++i) {
       mbar_init(&bars.st_full[i], 1);
       mbar_init(&bars.p_full[i], kSetWarps);
-      mbar_init(&bars.o_done[i], 1);
+      mbar_init(&bars.pv_done[i], 1);
     }
     mbar_init(&bars.drain, 1);
+    mbar_init(&bars.drain_s, 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -340,47 +342,15 @@ __global__ void __launch_bounds__(kMainThreads, 1)
       mbar_wait(&bars.kv_full[gg % kStages], (gg / kStages) & 1, &no_abort);
     for (int kk = max(0, kq - 2); kk < kq; ++kk) mbar_wait(&bars.q_full[kk & 1], (kk >> 1) & 1, &no_abort);
   } else if (warp == 1) {
-    // ---------------- MMA issuer: the whole warp waits, one elected lane issues ----------------
+    // ---------------- PV issue: the whole warp waits, one elected lane issues ----------------
+    // Two warps issue MMAs so that each one's barrier waits overlap the other's
+    // MMAs: this one O += P_g V_g in tile order, kSIssueWarp the S tiles. The
+    // S tile g lands in the buffer P_{g - kSets} occupies, so the S warp waits
+    // for pv_done (committed after that PV) before issuing it.
     {
       const bool leader = elect_one_sync();
-      constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, DH, false, true);
       bool ok = true;
-      // S cursor: item kS, tile tS within it, global gS (next item's count prefetched)
-      int kS = 0, tS = 0, gS = 0;
-      int nS = n_items > 0 ? item_ntiles(item_id(0)) : 0;
-      int nS_next = n_items > 1 ? item_ntiles(item_id(1)) : 0;
-      auto issue_next_s = [&]() -> bool {  // issues S_gS, advances the cursor; false when done
-        while (kS < n_items && tS >= nS) {  // leave finished (or empty) items, releasing their Q slot
-          if (nS == 0 && !(ok = mbar_wait_warp(&bars.q_full[kS & 1], (kS >> 1) & 1, &abort_flag))) return false;
-          if (leader) mma_commit(&bars.q_empty[kS & 1]);
-          __syncwarp();
-          ++kS;
-          tS = 0;
-          nS = nS_next;
-          nS_next = kS + 1 < n_items ? item_ntiles(item_id(kS + 1)) : 0;
-        }
-        if (kS >= n_items) return false;
-        if (tS == 0 && !(ok = mbar_wait_warp(&bars.q_full[kS & 1], (kS >> 1) & 1, &abort_flag))) return false;
-        const int st = gS % kStages;
-        if (!(ok = mbar_wait_warp(&bars.kv_full[st], (gS / kStages) & 1, &abort_flag))) return false;
-        tc_fence_after();
-        const uint64_t qd = sdesc(smem_u32(smem + C::kQOff + (kS & 1) * C::kTileBytes), 16, C::kSBO, C::kSwizzle);
-        const uint64_t kd = sdesc(smem_u32(smem + C::kKOff + st * C::kTileBytes), 16, C::kSBO, C::kSwizzle);
-        const uint32_t d = tmem + (gS % kSets) * 128;
-        if (leader) {
-#pragma unroll
-          for (int ks = 0; ks < DH / 16; ++ks) mma_ss(d, qd + ks * 2, kd + ks * 2, idesc_s, ks > 0 ? 1u : 0u);
-          mma_commit(&bars.st_full[gS % kSets]);
-        }
-        __syncwarp();
-        ++tS;
-        ++gS;
-        return true;
-      };
-      for (int i = 0; i < kSets && ok; ++i)
-        if (!issue_next_s()) break;
-      // PV cursor
       int kP = 0, g = 0;
       int nP_next = n_items > 0 ? item_ntiles(item_id(0)) : 0;
       for (; ok && kP < n_items; ++kP) {
@@ -399,12 +369,11 @@ __global__ void __launch_bounds__(kMainThreads, 1)
             for (int ks = 0; ks < RT_TILE / 16; ++ks)  // O += P_g V_g
               mma_ts(tmem + kOMain + ob * DH, tmem + set * 128 + ks * 8, vd + ks * C::kRowBytes, idesc_o,
                      (t > 0 || ks > 0) ? 1u : 0u);
-            mma_commit(&bars.o_done[set]);
+            mma_commit(&bars.pv_done[set]);
             mma_commit(&bars.kv_empty[g % kStages]);
             if (t == n - 1) mma_commit(&bars.item_done[ob]);
           }
           __syncwarp();
-          issue_next_s();  // into the S buffer P_g just left
         }
         if (n == 0) {
           if (leader) mma_commit(&bars.item_done[ob]);
@@ -416,6 +385,48 @@ __global__ void __launch_bounds__(kMainThreads, 1)
       volatile int no_abort = 0;
       mbar_wait_warp(&bars.drain, 0, &no_abort);
     }
+  } else if (warp == kSIssueWarp) {
+    // ---------------- S issue: item kS, tile tS within it, global tile gS ----------------
+    const bool leader = elect_one_sync();
+    constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false, false);
+    bool ok = true;
+    int kS = 0, tS = 0, gS = 0;
+    int nS = n_items > 0 ? item_ntiles(item_id(0)) : 0;
+    int nS_next = n_items > 1 ? item_ntiles(item_id(1)) : 0;
+    while (ok) {
+      while (kS < n_items && tS >= nS) {  // leave finished (or empty) items, releasing their Q slot
+        if (nS == 0 && !(ok = mbar_wait_warp(&bars.q_full[kS & 1], (kS >> 1) & 1, &abort_flag))) break;
+        if (leader) mma_commit(&bars.q_empty[kS & 1]);
+        __syncwarp();
+        ++kS;
+        tS = 0;
+        nS = nS_next;
+        nS_next = kS + 1 < n_items ? item_ntiles(item_id(kS + 1)) : 0;
+      }
+      if (!ok || kS >= n_items) break;
+      if (tS == 0 && !(ok = mbar_wait_warp(&bars.q_full[kS & 1], (kS >> 1) & 1, &abort_flag))) break;
+      const int st = gS % kStages;
+      if (!(ok = mbar_wait_warp(&bars.kv_full[st], (gS / kStages) & 1, &abort_flag))) break;
+      // S_gS overwrites P_{gS - kSets}: wait until the PV that reads it has completed
+      if (gS >= kSets && !(ok = mbar_wait_warp(&bars.pv_done[gS % kSets], ((gS / kSets) - 1) & 1, &abort_flag)))
+        break;
+      tc_fence_after();
+      const uint64_t qd = sdesc(smem_u32(smem + C::kQOff + (kS & 1) * C::kTileBytes), 16, C::kSBO, C::kSwizzle);
+      const uint64_t kd = sdesc(smem_u32(smem + C::kKOff + st * C::kTileBytes), 16, C::kSBO, C::kSwizzle);
+      const uint32_t d = tmem + (gS % kSets) * 128;
+      if (leader) {
+#pragma unroll
+        for (int ks = 0; ks < DH / 16; ++ks) mma_ss(d, qd + ks * 2, kd + ks * 2, idesc_s, ks > 0 ? 1u : 0u);
+        mma_commit(&bars.st_full[gS % kSets]);
+      }
+      __syncwarp();
+      ++tS;
+      ++gS;
+    }
+    if (leader) mma_commit(&bars.drain_s);
+    __syncwarp();
+    volatile int no_abort = 0;
+    mbar_wait_warp(&bars.drain_s, 0, &no_abort);
   } else if (warp < 2 + kEpiWarps) {
     // ---------------- epilogue warpgroup ----------------
     const int quad = warp & 3;
@@ -537,8 +548,8 @@ __global__ void __launch_bounds__(kMainThreads, 1)
           tmem_st16(sbuf + ch * 16, pk);
         }
         tmem_wait_st();
-        // the MMA thread has seen this set's previous P before this one completes
-        if (u > 0 && !(ok = mbar_wait_warp(&bars.o_done[set], (u - 1) & 1, &abort_flag))) break;
+        // S_gt completed after PV of this set's previous tile (one commit tracks
+        // every earlier MMA), so P_gt overwrites nothing that MMA still reads
         tc_fence_before();
         mbar_arrive_warp(&bars.p_full[set]);
       }
