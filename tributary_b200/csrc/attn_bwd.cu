@@ -941,7 +941,14 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
       tc_fence_after();
       uint32_t pk[16];
       const uint32_t st_addr = lane_base + kST0 + (i & 1) * 128 + col0;
-      softmax_phase_a_aux(st_addr, full, mk, scale_log2, pk);
+      // a 32 x 32 block of the tile with no live element: P = dS = 0, nothing to load or exponentiate
+      const bool zero = !full && __all_sync(0xFFFFFFFFu, mk == 0u);
+      if (zero) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) pk[e] = 0u;
+      } else {
+        softmax_phase_a_aux(st_addr, full, mk, scale_log2, pk);
+      }
       tmem_st16(st_addr, pk);  // P^T over the first 16 columns of this slice
       tmem_wait_st();
       tc_fence_before();
@@ -949,7 +956,12 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
       if (!(ok = mbar_wait_warp(&bars.dp_full, i & 1, &abort_flag))) break;
       tc_fence_after();
       uint32_t ds[16];
-      softmax_phase_b_aux(lane_base + kDPT + col0, pk, ds);
+      if (zero) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) ds[e] = 0u;
+      } else {
+        softmax_phase_b_aux(lane_base + kDPT + col0, pk, ds);
+      }
       // dS^T row `row`, queries [32 grp, 32 grp + 32): panel grp / 2, 16-byte
       // chunks (grp % 2) * 4 + c of the row, stored at chunk ^ (row % 8)
       uint8_t* drow = smem + C::kDS + (grp >> 1) * C::kDSPanel + row * 128;

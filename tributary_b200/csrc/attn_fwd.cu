@@ -525,6 +525,14 @@ __global__ void __launch_bounds__(kMainThreads, 1)
         const uint32_t mw[4] = {mk.x, mk.y, mk.z, mk.w};
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) {  // 32 columns; P of chunk ch lands in columns [16 ch, 16 ch + 16)
+          uint32_t pk[16];
+          // a 32 x 32 block with no live element: P = 0, nothing to load or exponentiate
+          if (!full && __all_sync(0xFFFFFFFFu, mw[ch] == 0u)) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) pk[e] = 0u;
+            tmem_st16(sbuf + ch * 16, pk);
+            continue;
+          }
           uint32_t r[32];
           tmem_ld32(sbuf + ch * 32, r);
           tmem_wait_ld();
@@ -532,7 +540,6 @@ __global__ void __launch_bounds__(kMainThreads, 1)
 #pragma unroll
             for (int e = 0; e < 32; ++e) r[e] = ((mw[ch] >> e) & 1u) ? r[e] : __float_as_uint(-INFINITY);
           }
-          uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
 #pragma unroll
