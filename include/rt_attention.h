@@ -159,7 +159,9 @@ int rt_heads_permute(const uint16_t* x, const uint16_t* perm, int32_t batch, int
  *   q, k, v [batch][heads][seq_len][head_dim] bf16;  head_dim in {32, 64}
  *   o       same shape, bf16
  *   lse     [batch][heads][seq_len] fp32, natural-log sum of exp over live keys
- * scale multiplies q.k (the reference divides by sqrt(head_dim)). */
+ * scale multiplies q.k (the reference divides by sqrt(head_dim)); it must be
+ * positive and finite (RT_ERR_INVALID_ARGUMENT otherwise), here and in the
+ * backward entry points. */
 int rt_attention_fwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, int32_t batch,
                      int32_t heads, int32_t seq_len, int32_t head_dim, float scale,
                      const rt_tile_plan* plan, uint16_t* o, float* lse, void* stream);

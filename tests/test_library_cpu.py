@@ -73,6 +73,16 @@ def test_argument_validation_before_device_work(lib):
     # unsupported head_dim is reported as such
     assert lib.rt_attention_fwd(fake, fake, fake, 1, 1, 128, 48, 1.0, ctypes.byref(plan),
                                 fake, fake, None) == _lib.RT_ERR_UNSUPPORTED
+    # a scale that is not positive and finite
+    for bad in (0.0, -0.125, float("nan"), float("inf")):
+        assert lib.rt_attention_fwd(fake, fake, fake, 1, 1, 128, 64, bad, ctypes.byref(plan),
+                                    fake, fake, None) == _lib.RT_ERR_INVALID_ARGUMENT
+        assert lib.rt_attention_bwd(fake, fake, fake, fake, fake, fake, 1, 1, 128, 64, bad,
+                                    ctypes.byref(plan), fake, fake, fake, fake, 1 << 20,
+                                    None) == _lib.RT_ERR_INVALID_ARGUMENT
+        assert lib.rt_attention_bwd_noalloc(fake, fake, fake, fake, fake, fake, 1, 1, 128, 64, bad,
+                                            ctypes.byref(plan), fake, fake, fake,
+                                            None) == _lib.RT_ERR_INVALID_ARGUMENT
     # misaligned tensor
     odd = ctypes.c_void_p((1 << 21) + 2)
     assert lib.rt_attention_fwd(odd, fake, fake, 1, 1, 128, 64, 1.0, ctypes.byref(plan),

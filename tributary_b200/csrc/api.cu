@@ -258,6 +258,8 @@ int rt_attention_fwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, in
   if (batch < 0 || heads < 0 || seq_len < 0 || seq_len > 65536 || batch > 65535 || heads > 65535)
     return RT_ERR_INVALID_ARGUMENT;
   if (head_dim != 32 && head_dim != 64) return RT_ERR_UNSUPPORTED;
+  // masked logits enter as -inf times the scale, and the fused backward divides by it
+  if (!(scale > 0.f) || !(scale < INFINITY)) return RT_ERR_INVALID_ARGUMENT;
   if (batch == 0 || heads == 0 || seq_len == 0) return RT_OK;
   if (!plan_matches(plan, batch, seq_len)) return RT_ERR_INVALID_ARGUMENT;
   if (!q || !k || !v || !o || !lse) return RT_ERR_INVALID_ARGUMENT;
@@ -293,6 +295,8 @@ int rt_attention_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, co
   if (batch < 0 || heads < 0 || seq_len < 0 || seq_len > 65536 || batch > 65535 || heads > 65535)
     return RT_ERR_INVALID_ARGUMENT;
   if (head_dim != 32 && head_dim != 64) return RT_ERR_UNSUPPORTED;
+  // masked logits enter as -inf times the scale, and the fused backward divides by it
+  if (!(scale > 0.f) || !(scale < INFINITY)) return RT_ERR_INVALID_ARGUMENT;
   if (batch == 0 || heads == 0 || seq_len == 0) return RT_OK;
   if (!plan_matches(plan, batch, seq_len)) return RT_ERR_INVALID_ARGUMENT;
   if (!q || !k || !v || !o || !d_o || !lse || !dq || !dk || !dv || !workspace)

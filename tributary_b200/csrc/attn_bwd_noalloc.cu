@@ -64,6 +64,8 @@ extern "C" int rt_attention_bwd_noalloc(const uint16_t* q, const uint16_t* k, co
   if (batch < 0 || heads < 0 || seq_len < 0 || seq_len > 65536 || batch > 65535 || heads > 65535)
     return RT_ERR_INVALID_ARGUMENT;
   if (head_dim != 32 && head_dim != 64) return RT_ERR_UNSUPPORTED;
+  // masked logits enter as -inf times the scale, and the fused backward divides by it
+  if (!(scale > 0.f) || !(scale < INFINITY)) return RT_ERR_INVALID_ARGUMENT;
   if (batch == 0 || heads == 0 || seq_len == 0) return RT_OK;
   const long long padded_rows =
       (long long)batch * heads * ((long long)(seq_len + RT_TILE - 1) / RT_TILE) * RT_TILE;
