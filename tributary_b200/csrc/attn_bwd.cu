@@ -739,9 +739,28 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
     fence_proxy_async_smem();
   }
 
+  // Q, dO and the row-statistic rows of the i-th live q-tile into ring stage i % kStages
+  auto load_tile = [&](int i, int qtile) {
+    const int s = i % C::kStages;
+    mbar_arrive_expect_tx(&bars.ring_full[s], 2 * C::kTileBytes + C::kAuxTileBytes);
+    tma_load_3d(smem + C::kR0 + s * C::kTileBytes, &tm_q, &bars.ring_full[s], 0, qtile * RT_TILE, bh);
+    tma_load_3d(smem + C::kR1 + s * C::kTileBytes, &tm_do, &bars.ring_full[s], 0, qtile * RT_TILE, bh);
+    tma_load_2d(smem + C::kFAux + s * C::kAuxTileBytes, &tm_aux, &bars.ring_full[s], 0, bh * Sp + qtile * RT_TILE);
+  };
+  // The producer thread starts K, V and the first ring stages as soon as the
+  // barriers exist, so their latency overlaps the TMEM allocation, the list
+  // copy and the block barrier below (the list entries come from global
+  // memory here; s_list is not complete yet).
+  const int n_early = min(n_tiles, C::kStages);
   if (threadIdx.x == 0) {
     abort_flag = 0;
     init_barriers(bars, C::kStages);
+    if (n_tiles > 0) {
+      mbar_arrive_expect_tx(&bars.res_full, 2 * C::kTileBytes);
+      tma_load_3d(smem + C::kA0, &tm_k, &bars.res_full, 0, kt * RT_TILE, bh);
+      tma_load_3d(smem + C::kA1, &tm_v, &bars.res_full, 0, kt * RT_TILE, bh);
+      for (int i = 0; i < n_early; ++i) load_tile(i, plan.k2q_idx[list_begin + i] & 0x7FFFFFFF);
+    }
   }
   if (warp == 0) {
     tmem_alloc(&tmem_base_s, kTmemCols);
@@ -754,19 +773,11 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
 
   if (warp == 0) {
     if (lane == 0 && n_tiles > 0) {
-      mbar_arrive_expect_tx(&bars.res_full, 2 * C::kTileBytes);
-      tma_load_3d(smem + C::kA0, &tm_k, &bars.res_full, 0, kt * RT_TILE, bh);
-      tma_load_3d(smem + C::kA1, &tm_v, &bars.res_full, 0, kt * RT_TILE, bh);
-      int i = 0;
+      int i = n_early;
       for (; i < n_tiles; ++i) {
         const int s = i % C::kStages;
-        if (i >= C::kStages && !mbar_wait(&bars.ring_empty[s], ((i / C::kStages) - 1) & 1, &abort_flag)) break;
-        const int qtile = s_list[i] & 0x7FFFFFFF;
-        mbar_arrive_expect_tx(&bars.ring_full[s], 2 * C::kTileBytes + C::kAuxTileBytes);
-        tma_load_3d(smem + C::kR0 + s * C::kTileBytes, &tm_q, &bars.ring_full[s], 0, qtile * RT_TILE, bh);
-        tma_load_3d(smem + C::kR1 + s * C::kTileBytes, &tm_do, &bars.ring_full[s], 0, qtile * RT_TILE, bh);
-        tma_load_2d(smem + C::kFAux + s * C::kAuxTileBytes, &tm_aux, &bars.ring_full[s], 0,
-                    bh * Sp + qtile * RT_TILE);
+        if (!mbar_wait(&bars.ring_empty[s], ((i / C::kStages) - 1) & 1, &abort_flag)) break;
+        load_tile(i, s_list[i] & 0x7FFFFFFF);
       }
       volatile int no_abort = 0;
       for (int ii = max(0, i - C::kStages); ii < i; ++ii)
@@ -919,7 +930,10 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
         bulk_commit_group();
       }
     }
-    if (lane == 0) bulk_wait_all();  // every reduce this warp issued has completed
+    // The reduces have read this warp's staging slot (the shared memory may
+    // not be released before); their additions into dq_acc complete with
+    // the grid, before any later work on the stream reads it.
+    if (lane == 0) bulk_wait_read_all();
   } else {
     const int quad = warp & 3;
     const int grp = (warp - 2) >> 2;  // column group: queries [32 grp, 32 grp + 32) of every tile
