@@ -44,21 +44,27 @@ struct Cfg {
   static constexpr int kDynSmem = (kSmemBytes + 1024) > 118 * 1024 ? (kSmemBytes + 1024) : 118 * 1024;
   // Fused dK/dV/dQ kernel. After the Q / dO ring: a ring of row-statistic
   // operand tiles [128 queries][16 bf16] (32-byte swizzle), then two constant
-  // tiles of the same shape (ones in columns 0-1, resp. 2-3), then the dS^T
-  // tile [2 panels][128 keys][64 queries] bf16 (128-byte swizzle), then one
-  // dQ staging slot per reduce warp: DH / 32 boxes [32 rows][32 fp32]
-  // (128-byte swizzle).
+  // 8-row tiles of that shape (ones in columns 0-1, resp. 2-3) that every
+  // 8-row group of the MMA's A operand reads (stride 0), then the dS^T tile
+  // [2 panels][128 keys][64 queries] bf16 (128-byte swizzle), then one dQ
+  // staging ring per reduce warp: DH / 32 + 1 boxes [32 rows][32 fp32]
+  // (128-byte swizzle), one box more than a tile's partial needs, so that
+  // a box is rewritten only once the reduce issued from it three (DH = 64)
+  // or two (DH = 32) boxes earlier has read it.
   static constexpr int kAuxTileBytes = RT_TILE * 32;
   static constexpr int kFAux = kR1 + kStages * kTileBytes;
   static constexpr int kFOnes = kFAux + kStages * kAuxTileBytes;
-  static constexpr int kDS = kFOnes + 2 * kAuxTileBytes;
+  static constexpr int kDS = (kFOnes + 512 + 1023) / 1024 * 1024;
   static constexpr int kDSPanel = RT_TILE * 128;
   static constexpr int kStg = kDS + 2 * kDSPanel;
   static constexpr int kStgBox = 32 * 32 * 4;
-  static constexpr int kStgSlot = (DH / 32) * kStgBox;
+  static constexpr int kStgBoxesPerTile = DH / 32;
+  static constexpr int kStgRing = kStgBoxesPerTile + 1;
+  static constexpr int kStgSlot = kStgRing * kStgBox;
   static constexpr int kStgBytes = 4 * kStgSlot;
   static constexpr int kDynSmemFused = kStg + kStgBytes + 1024;
   static_assert(kFAux % 1024 == 0 && kDS % 1024 == 0 && kStg % 1024 == 0, "fused layout alignment");
+  static_assert(kDynSmemFused + 2304 <= 227 * 1024, "fused layout and static shared memory exceed 227 KB");
 };
 
 constexpr int kMaxTiles = 65536 / RT_TILE;
@@ -722,12 +728,12 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
   const int n_tiles = plan.k2q_ptr[col_list + 1] - list_begin;
   const int Sp = T * RT_TILE;
   for (int i = threadIdx.x; i < n_tiles; i += kThreadsFused) s_list[i] = plan.k2q_idx[list_begin + i];
-  // Constant ones tiles [2][128 rows][16 bf16], 32-byte swizzle (the 16-byte
+  // Constant ones tiles [2][8 rows][16 bf16], 32-byte swizzle (the 16-byte
   // half j of row r sits at half j ^ ((r >> 2) & 1)): tile 0 has 1.0 in
-  // columns 0-1, tile 1 in columns 2-3. 512 threads write 16 bytes each.
-  if (threadIdx.x < 2 * C::kAuxTileBytes / 16) {
+  // columns 0-1, tile 1 in columns 2-3. 32 threads write 16 bytes each.
+  if (threadIdx.x < 32) {
     const int off = threadIdx.x * 16;
-    const int tile = off / C::kAuxTileBytes, row = (off % C::kAuxTileBytes) / 32, half = (off % 32) / 16;
+    const int tile = off >> 8, row = (off & 255) >> 5, half = (off & 31) >> 4;
     const bool logical0 = (half ^ ((row >> 2) & 1)) == 0;
     const uint32_t ones = 0x3F803F80u;  // two bf16 1.0
     uint4 val = make_uint4(0u, 0u, 0u, 0u);
@@ -799,8 +805,9 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
       const uint64_t k_mn = sdesc(smem_u32(smem + C::kA0), 0, C::kSBO, C::kSwizzle);
       const uint64_t ds_mn = sdesc(smem_u32(smem + C::kDS), C::kDSPanel, 1024, SW_128B);
       const uint64_t ds_kmaj = sdesc(smem_u32(smem + C::kDS), 16, 1024, SW_128B);
-      const uint64_t ones_s = sdesc(smem_u32(smem + C::kFOnes), 16, 256, SW_32B);
-      const uint64_t ones_dp = sdesc(smem_u32(smem + C::kFOnes + C::kAuxTileBytes), 16, 256, SW_32B);
+      // the 8-row ones tiles with a zero stride between 8-row groups: every group reads the same rows
+      const uint64_t ones_s = sdesc(smem_u32(smem + C::kFOnes), 16, 0, SW_32B);
+      const uint64_t ones_dp = sdesc(smem_u32(smem + C::kFOnes + 256), 16, 0, SW_32B);
       auto ring_desc = [&](int base, int i, uint32_t lbo) {
         return sdesc(smem_u32(smem + base + (i % C::kStages) * C::kTileBytes), lbo, C::kSBO, C::kSwizzle);
       };
@@ -896,11 +903,15 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
   } else if (warp >= 2 + kSoftmaxThreads / 32) {
     // ---------------- dQ reduce warps ----------------
     // Warp w reads TMEM lanes [32 (w % 4), +32): queries 32 quad + lane of the
-    // tile, all DH columns. Its slot holds DH / 32 boxes [32 rows][32 fp32],
-    // 16-byte chunk c of row r at chunk c ^ (r % 8) (the 128-byte swizzle).
+    // tile, all DH columns. Its slot is a ring of kStgRing boxes [32
+    // rows][32 fp32], 16-byte chunk c of row r at chunk c ^ (r % 8) (the
+    // 128-byte swizzle). Each box is reduced as its own bulk group; before
+    // a box is rewritten, only the reduce issued kStgRing boxes earlier (the
+    // box's previous use) must have read it, not every earlier one.
     const int quad = warp & 3;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     uint8_t* slot = smem + C::kStg + (warp - 2 - kSoftmaxThreads / 32) * C::kStgSlot;
+    int rb = 0;  // ring position of the next box
     for (int t = 0; t < n_tiles; ++t) {
       if (!mbar_wait_warp(&bars.dq_ready, t & 1, &abort_flag)) break;
       tc_fence_after();
@@ -911,23 +922,25 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive_warp(&bars.dq_drained);
-      if (lane == 0) bulk_wait_read_all();  // this warp's previous reduces have read the slot
-      __syncwarp();
+      const int row0 = bh * Sp + (s_list[t] & 0x7FFFFFFF) * RT_TILE + quad * 32;
 #pragma unroll
-      for (int x = 0; x < DH / 32; ++x) {
-        uint8_t* srow = slot + x * C::kStgBox + lane * 128;
+      for (int x = 0; x < C::kStgBoxesPerTile; ++x) {
+        uint8_t* box = slot + rb * C::kStgBox;
+        // at most kStgRing - 1 groups still reading: the box's previous reduce is done with it
+        if (lane == 0) bulk_wait_read<C::kStgRing - 1>();
+        __syncwarp();
+        uint8_t* srow = box + lane * 128;
 #pragma unroll
         for (int c = 0; c < 8; ++c)
           *reinterpret_cast<uint4*>(srow + ((c ^ (lane & 7)) << 4)) =
               make_uint4(r[x * 32 + 4 * c], r[x * 32 + 4 * c + 1], r[x * 32 + 4 * c + 2], r[x * 32 + 4 * c + 3]);
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        const int row0 = bh * Sp + (s_list[t] & 0x7FFFFFFF) * RT_TILE + quad * 32;
-#pragma unroll
-        for (int x = 0; x < DH / 32; ++x) tma_reduce_add_2d(&tm_acc, slot + x * C::kStgBox, x * 32, row0);
-        bulk_commit_group();
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_2d(&tm_acc, box, x * 32, row0);
+          bulk_commit_group();
+        }
+        rb = rb + 1 == C::kStgRing ? 0 : rb + 1;
       }
     }
     // The reduces have read this warp's staging slot (the shared memory may

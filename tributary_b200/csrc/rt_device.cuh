@@ -161,6 +161,12 @@ __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bu
 // The issuing thread's bulk groups have completed (writes performed).
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// Until at most N of this thread's most recent bulk groups are still reading their source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
