@@ -54,7 +54,7 @@ FLOPS_PER_LIVE_TILE = {"fwd": 4, "bwd": 10}  # x 128^2 x Dh per live (b, h, tile
 # capture of this workload (summarised under profiles/); about the same for
 # every mask kind: q, k, v, dO and the row statistics read once, dK and dV
 # written once, plus the fp32 dQ accumulator's L2 misses under the reduce-adds.
-NCU_DKDVQ_TRAFFIC = {"rt_attn_fwd_bwd_b8_s4096_h16_d64": 647.2e6}
+NCU_DKDVQ_TRAFFIC = {"rt_attn_fwd_bwd_b8_s4096_h16_d64": 647.0e6}
 
 
 def measured_peaks():
