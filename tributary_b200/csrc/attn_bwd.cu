@@ -943,10 +943,10 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
         rb = rb + 1 == C::kStgRing ? 0 : rb + 1;
       }
     }
-    // The reduces have read this warp's staging slot (the shared memory may
-    // not be released before); their additions into dq_acc complete with
-    // the grid, before any later work on the stream reads it.
-    if (lane == 0) bulk_wait_read_all();
+    // Every reduce this warp issued has completed, its additions into dq_acc
+    // included: a wait for the reads alone would let the block exit with
+    // additions in flight, and nothing orders those before dq_convert_kernel.
+    if (lane == 0) bulk_wait_all();
   } else {
     const int quad = warp & 3;
     const int grp = (warp - 2) >> 2;  // column group: queries [32 grp, 32 grp + 32) of every tile
