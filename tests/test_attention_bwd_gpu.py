@@ -134,3 +134,27 @@ def test_backward_repeated_under_concurrent_copies(cuda_lib):
         torch.cuda.synchronize()
         assert device_status() == 0, it
         assert torch.equal(dk, ref[1]) and torch.equal(dv, ref[2]), it
+        # dQ: reduction order moves an element by at most about one bf16 unit of
+        # its own size; a lost partial would move whole rows. (Element-wise
+        # relative error is no measure here: a million sums of 16 partials
+        # include elements that cancel to near zero.)
+        err = max_rel(from_bf16_tensor(dq), from_bf16_tensor(ref[0]))
+        assert err < 2.0 ** -7, (it, err)
+
+
+@pytest.mark.parametrize("dh", [32, 64])
+def test_backward_dq_complete_when_the_call_returns(cuda_lib, dh):
+    """dQ is summed by asynchronous TMA reduce-adds into an fp32 buffer that
+    the next kernel on the stream converts to bf16; every addition must have
+    landed by then. A small case, where all blocks finish at about the same
+    time, is where an addition still in flight at the end of the fused kernel
+    would show, so it runs many times against the oracle."""
+    from tributary_b200.attention import attention_bwd, attention_fwd, device_status
+    c = Case(GENS["cfgA"], 0, h=2, dh=dh, seed=2004 + dh)
+    dq_ref = c.oracle_bwd()[0]
+    o, lse = attention_fwd(c.qd, c.kd, c.vd, c.plan, c.scale)
+    for it in range(40):
+        dq, _, _ = attention_bwd(c.qd, c.kd, c.vd, o, lse, c.dod, c.plan, c.scale)
+        assert device_status() == 0, it
+        err = max_rel(from_bf16_tensor(dq), dq_ref)
+        assert err < TOL_OUT, (it, err)
