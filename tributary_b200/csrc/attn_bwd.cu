@@ -5,14 +5,20 @@
 //   delta_i = sum_d dO_id O_id                         (row_stats_kernel)
 //   p_ij    = mask_ij ? exp(s_ij - lse_i) : 0,  s = scale q k^T
 //   dP      = dO V^T ; dS = P o (dP - delta)
-//   dQ      = scale * dS K                             (dq_kernel: thread = query)
-//   dV      = P^T dO ; dK = scale * dS^T Q             (dkdv_kernel: thread = key)
+//   dQ      = scale * dS K
+//   dV      = P^T dO ; dK = scale * dS^T Q
 //
-// Both gradient kernels recompute P from lse, iterate only live tiles (q2k
-// list for dQ, k2q list for dK/dV), double-buffer S in tensor memory so the
-// next tile's QK^T overlaps the exponentials, and accumulate in TMEM, so every output
-// element is written once by one CTA: results are deterministic, with no
-// atomics; the only scratch is the padded row-statistics workspace.
+// Two paths, both over live tiles only, recomputing P from lse with S
+// double-buffered in tensor memory:
+// - rt_attention_bwd: dkdvq_kernel, one CTA per (b, h, k-tile) over its k2q
+//   list. It computes S, dP and P once per tile and yields all three
+//   gradients: dK and dV accumulate in TMEM and are written once, while dQ
+//   partials are reduce-added (TMA) into an fp32 workspace accumulator that
+//   dq_convert_kernel scales and rounds. dQ is reproducible to fp32 rounding.
+// - rt_attention_bwd_noalloc: dkdv_kernel (k2q lists, thread = key) and
+//   dq_kernel (q2k lists, thread = query). Each output element is written once
+//   by one CTA, so all three gradients are bit-reproducible; the only scratch
+//   is the padded row statistics.
 #include "rt_device.cuh"
 #include "rt_internal.h"
 
