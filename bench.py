@@ -333,60 +333,116 @@ def barrier(world):
     torch.cuda.synchronize()
 
 
-def cpu_sample(cfg, seed, budget_s=15.0, threads=None):
-    """Time the numpy restatement (fp32 dense masked attention fwd + analytic
-    bwd) on a bounded sample: batch element 0, `hs` heads, each mask kind.
-    Returns (cells_per_s, sample description, threads used)."""
+def oracle_sample_batch(cfg, seed):
+    """Sample 0 of the workload's batch and its four cell orders, built by the
+    oracle's numpy restatement of the generator and of the sampler's orders
+    (the same draws as the library's generator, pinned equal by the tests), so
+    that the CPU legs load nothing of the library."""
     from oracle import rt_oracle as orc  # CPU baseline leg
-    bt = make_metadata(dict(cfg, B=1), seed)
-    S, H, Dh = cfg["S"], cfg["H"], cfg["Dh"]
-    rng = np.random.default_rng(seed)
-    hs = 2 if S >= 4096 else min(H, 4)
-    q, k, v, do = (rng.standard_normal((1, hs, S, Dh)).astype(np.float32) for _ in range(4))
-    scale = np.float32(1.0 / math.sqrt(Dh))
-    masks = []
-    for kind in range(4):
-        m = orc.mask_for_kind(kind, bt["seq_row_ids"], bt["fk_adj"], bt["column_ids"], bt["is_padding"])
-        masks.append(orc.permute_mask(m, perm_for(bt, kind)))
+    return orc.make_batch(seed, 1, cfg["S"], cfg["tables"], cfg["cells_lo"], cfg["cells_hi"], cfg["p_fk"],
+                          cfg["pad"], max_parents=cfg["max_parents"])
+
+
+class CpuSample:
+    """The numpy restatement of the reference math (fp32 dense masked
+    attention, confluence/confluence/layers.py:83-97, plus its analytic
+    backward) on a bounded sample of the workload: batch element 0 of the
+    same seeded batch, `hs` of the H heads, every mask kind under its own cell
+    order. One call = forward + backward of every kind and sampled head, the
+    (kind, head) problems spread over all host cores (one BLAS thread each)."""
+
+    def __init__(self, cfg, seed):
+        from concurrent.futures import ThreadPoolExecutor
+        from oracle import rt_oracle as orc  # CPU baseline leg
+        self.orc = orc
+        bt = oracle_sample_batch(cfg, seed)
+        S, H, Dh = cfg["S"], cfg["H"], cfg["Dh"]
+        self.S, self.H, self.B = S, H, cfg["B"]
+        self.cores = len(os.sched_getaffinity(0))
+        # enough (kind, head) problems to occupy every core once
+        self.hs = min(H, max(2, -(-self.cores // 4)))
+        rng = np.random.default_rng(seed)
+        self.q, self.k, self.v, self.do = (rng.standard_normal((1, self.hs, S, Dh)).astype(np.float32)
+                                           for _ in range(4))
+        self.scale = np.float32(1.0 / math.sqrt(Dh))
+        self.masks = []
+        for kind in range(4):
+            m = orc.mask_for_kind(kind, bt["seq_row_ids"], bt["fk_adj"], bt["column_ids"], bt["is_padding"])
+            self.masks.append(orc.permute_mask(m, orc.perm_for_kind(bt, kind)))
+        self.pool = ThreadPoolExecutor(max_workers=self.cores)
+
+    def cells_per_call(self):
+        # one attention call over all H heads counts S cells, per kind
+        return 4 * self.S * self.hs / self.H
+
+    def _one(self, kind_head):
+        kind, h = kind_head
+        sel = (slice(0, 1), slice(h, h + 1))
+        q, k, v, do = self.q[sel], self.k[sel], self.v[sel], self.do[sel]
+        o, _ = self.orc.attention_fwd(q, k, v, self.masks[kind], self.scale)
+        self.orc.attention_bwd(q, k, v, o, do, self.masks[kind], self.scale)
+
+    def call(self):
+        from threadpoolctl import threadpool_limits
+        with threadpool_limits(limits=1):
+            list(self.pool.map(self._one, [(kd, h) for kd in range(4) for h in range(self.hs)]))
+
+    def describe(self, calls):
+        return (f"b=1 of {self.B}, {self.hs} of {self.H} heads, {calls} fwd+bwd calls of each of the 4 kinds; "
+                f"numpy fp32 restatement of the reference path, (kind, head) problems on {self.cores} threads "
+                f"(jax/XLA-CPU not installable)")
+
+
+def cpu_sample(cfg, seed, budget_s=15.0):
+    """(cells/s, sample description) of CpuSample over about budget_s seconds."""
+    smp = CpuSample(cfg, seed)
     t0 = time.perf_counter()
     calls = 0
-    while True:
-        for kind in range(4):
-            o, lse = orc.attention_fwd(q, k, v, masks[kind], scale)
-            orc.attention_bwd(q, k, v, o, do, masks[kind], scale)
-            calls += 1
-        if time.perf_counter() - t0 > budget_s:
-            break
+    while calls == 0 or time.perf_counter() - t0 < budget_s:
+        smp.call()
+        calls += 1
     dt = time.perf_counter() - t0
-    cells = calls * S * hs / H  # a call over all H heads counts S cells
-    return cells / dt, f"b=1 of {cfg['B']}, {hs} of {H} heads, {calls} fwd+bwd calls over the 4 kinds", threads
+    return calls * smp.cells_per_call() / dt, smp.describe(calls)
+
+
+def config_record(cfg, world):
+    """The `config` object both arms print for the attention workload."""
+    return {"workload": cfg["name"], "B": cfg["B"], "S": cfg["S"], "H": cfg["H"], "Dh": cfg["Dh"],
+            "masks": list(KIND_NAMES),
+            "generator": {k: cfg[k] for k in ("tables", "cells_lo", "cells_hi", "p_fk", "max_parents", "pad")},
+            "l2": "inputs > L2 (q/k/v/dO distinct per kind, %.2f GB resident)" % (
+                16 * cfg["B"] * cfg["H"] * cfg["S"] * cfg["Dh"] * 2 / 1e9),
+            "parallelism": f"batch-sharded x{world}: attention with no collective; training step dp{world} "
+                           f"with NCCL gradient all-reduce (train_step)"}
 
 
 def run_reference_arm(args, cfg):
+    """The reference's CPU path: the oracle port (the reference's JAX path on
+    XLA-CPU cannot be installed here) on the host cores, rank 0 only. A step
+    is one bounded sample of the workload (CpuSample.call); ms_per_step is the
+    time a step actually took and value the sample's cells per second."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     cores = len(os.sched_getaffinity(0))
-    values = []
-    per_step = max(1.0, min(8.0, 150.0 / max(1, args.steps)))
+    smp = CpuSample(cfg, 1000)
     for _ in range(args.warmup):
-        cpu_sample(cfg, 1234, budget_s=1.0)
+        smp.call()
+    t0 = time.perf_counter()
     for _ in range(args.steps):
-        v, sample, _ = cpu_sample(cfg, 1234, budget_s=per_step)
-        values.append(v)
-    value = statistics.median(values)
-    ms_per_step = 1e3 * 4 * cfg["B"] * cfg["S"] / value
+        smp.call()
+    dt = time.perf_counter() - t0
+    value = args.steps * smp.cells_per_call() / dt
     line = {
         "impl": "reference", "metric": "rt_attention_fwd_bwd_cells_per_s", "value": value,
-        "unit": "cells/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "unit": "cells/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": {"workload": cfg["name"], "B": cfg["B"], "S": cfg["S"], "H": cfg["H"], "Dh": cfg["Dh"],
-                   "masks": list(KIND_NAMES)},
+        "config": config_record(cfg, world),
+        "sample": smp.describe(1) + " per step",
         "cpu_baseline": {"value": value, "unit": "cells/s", "cores": cores, "kind": "port",
-                         "sample": sample + "; numpy fp32 restatement of the reference path "
-                                   "(jax/XLA-CPU not installable)"},
+                         "sample": smp.describe(args.steps)},
         "e2e": {"value": value, "unit": "cells/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -463,6 +519,7 @@ def run_our_arm(args, cfg):
         raise RuntimeError(f"device status error {status}")
 
     cfgd = wl.cfg
+    launches = wl.launches_per_step() * args.steps
     cells_step = 4 * cfgd["B"] * cfgd["S"]  # 4 attention calls (one per mask kind) per step
     value = world * cells_step / (step_ms * 1e-3)
     flops = wl.live_tile_flops()
@@ -472,20 +529,19 @@ def run_our_arm(args, cfg):
     bwd_tf = flops["bwd"] / (part_ms["bwd"] * 1e-3) / 1e12
     fwd_tf = flops["fwd"] / (part_ms["fwd"] * 1e-3) / 1e12
     densities = {KIND_NAMES[i]: wl.nnz[i] / (cfgd["B"] * wl.tiles * wl.tiles) for i in range(4)}
+    del wl
+    torch.cuda.empty_cache()
+    train = None
+    if not args.no_train:
+        train = measure_train(dict(CONFIGS["d"]), args.train_steps, 3, world, rank, local)
     if rank == 0:
         line = {
             "metric": "rt_attention_fwd_bwd_cells_per_s", "value": value, "unit": "cells/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": cfgd["name"], "B": cfgd["B"], "S": cfgd["S"], "H": cfgd["H"],
-                       "Dh": cfgd["Dh"], "masks": list(KIND_NAMES),
-                       "generator": {k: cfgd[k] for k in ("tables", "cells_lo", "cells_hi", "p_fk",
-                                                          "max_parents", "pad")},
-                       "live_tile_density": densities,
-                       "l2": "inputs > L2 (q/k/v/dO distinct per kind, %.2f GB resident)" % (
-                           16 * cfgd["B"] * cfgd["H"] * cfgd["S"] * cfgd["Dh"] * 2 / 1e9),
-                       "parallelism": f"batch-sharded x{world} (replicas, no collective)"},
+            "config": config_record(cfgd, world),
+            "live_tile_density": densities,
             "tflops_live_tiles": achieved_tf,
             "frac_of_bf16_peak": achieved_tf / peak_tf,
             "breakdown_ms_per_step": part_ms,
@@ -504,11 +560,13 @@ def run_our_arm(args, cfg):
                          "fwd_plus_bwd": {"achieved": achieved_tf, "frac": achieved_tf / peak_tf}},
             "e2e": {"value": world * cells_step / (e2e_ms * 1e-3), "unit": "cells/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": wl.launches_per_step() * args.steps,
+            "gpu_launches": launches,
             "clocks": clocks,
         }
+        if train is not None:
+            line["train_step"] = train
         if not args.no_cpu_baseline:
-            v, sample, _ = cpu_sample(cfgd, 1234, budget_s=args.cpu_seconds)
+            v, sample = cpu_sample(cfgd, 1000, budget_s=args.cpu_seconds)
             line["cpu_baseline"] = {"value": v, "unit": "cells/s", "cores": len(os.sched_getaffinity(0)),
                                     "kind": "port", "sample": sample}
         print(json.dumps(line), flush=True)
@@ -564,52 +622,131 @@ def train_flops(model, cfg, masks, tokens):
     return lin_flops + logits + attn * cfg["layers"], attn * cfg["layers"]
 
 
+class TrainRun:
+    """The config-d training step on this rank's GPU: its own B=32 shard of
+    cells, a replica with the same initial weights on every rank, and a
+    TrainStep whose gradient buckets are all-reduced over NCCL (reduce=True)
+    or kept local (reduce=False, the single-GPU step on the same device)."""
+
+    def __init__(self, cfg, rank, dev, reduce=True):
+        import torch
+        from tributary_b200.encoder import RTEncoder
+        from tributary_b200.train import TrainStep
+        self.cfg = cfg
+        cells = make_train_cells(cfg, 1000 + rank)
+        self.host = {k: v.pin_memory() for k, v in cells_to_host_tensors(cells).items()}
+        self.d = {k: v.to(dev) for k, v in self.host.items()}
+        for k in ("target_stype", "cat_start"):
+            self.d[k] = cells[k]
+        self.col = torch.from_numpy(cells["col_table"]).to(dev)
+        self.cat = torch.from_numpy(cells["cat_table"]).to(dev)
+        torch.manual_seed(1234)  # identical initial weights on every rank
+        self.model = RTEncoder(encoder_config(cfg)).to(dev)
+        self.step = TrainStep(self.model, reduce=reduce)
+
+    def __call__(self):
+        from tributary_b200.train import build_masks
+        return self.step(self.d, build_masks(self.d, TRAIN_KINDS), self.col, self.cat)
+
+    def timed(self, steps, world, finish_events=False):
+        """Device ms per step over `steps` steps (max over ranks) and, with
+        finish_events, the mean exposed all-reduce ms (max over ranks)."""
+        import torch
+        barrier(world)
+        self.step.finish_events = [] if finish_events else None
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            loss = self()
+        e1.record()
+        barrier(world)
+        ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+        exposed = None
+        if finish_events:
+            exposed = max_over_ranks(sum(a.elapsed_time(b) for a, b in self.step.finish_events) / steps, world)
+            self.step.finish_events = None
+        return ms, exposed, loss
+
+    def checksum_spread(self, world):
+        """Relative spread over ranks of the sum of all parameters: 0 when the
+        replicas stayed identical (same weights, same averaged gradients)."""
+        import torch
+        with torch.no_grad():
+            chk = torch.stack([p.double().sum() for p in self.model.parameters()]).sum().reshape(1)
+        if world == 1:
+            return 0.0
+        import torch.distributed as dist
+        allc = [torch.zeros_like(chk) for _ in range(world)]
+        dist.all_gather(allc, chk)
+        vals = torch.cat(allc)
+        return float((vals.max() - vals.min()).abs() / vals.abs().max().clamp_min(1e-30))
+
+
+def measure_train(cfg, steps, warmup, world, rank, local):
+    """The data-parallel training step (config d) at this world size: ms per
+    step with the overlapped NCCL gradient all-reduce, the all-reduce time the
+    backward does not hide, and the same step without the collective on the
+    same GPUs (its ratio to the data-parallel step is the weak-scaling
+    efficiency against one GPU). Every rank calls it (collectives inside)."""
+    import torch
+    from tributary_b200.attention import device_status
+    dev = torch.device("cuda", local)
+    run = TrainRun(cfg, rank, dev, reduce=True)
+    for _ in range(warmup):
+        run()
+    dp_ms, exposed_ms, loss = run.timed(steps, world, finish_events=True)
+    spread = run.checksum_spread(world)
+    loss_val = float(loss.item())
+    grad_bytes = sum(run.step.buckets.bucket_sizes)
+    n_buckets = len(run.step.buckets.buffers)
+    del run
+    torch.cuda.empty_cache()
+    solo = TrainRun(cfg, rank, dev, reduce=False)
+    for _ in range(warmup):
+        solo()
+    solo_ms, _, _ = solo.timed(steps, world)
+    del solo
+    torch.cuda.empty_cache()
+    status = device_status(reset=True)
+    if status != 0 or not math.isfinite(loss_val):
+        raise RuntimeError(f"training step: device status {status}, loss {loss_val}")
+    tokens = cfg["B"] * cfg["S"]
+    return {"workload": cfg["name"], "n_gpus": world, "B_per_gpu": cfg["B"], "S": cfg["S"], "steps": steps,
+            "ms_per_step": dp_ms, "tokens_per_s": world * tokens / (dp_ms * 1e-3),
+            "allreduce": {"what": f"NCCL all-reduce (average) of {grad_bytes / 1e6:.0f} MB fp32 gradients "
+                                  f"in {n_buckets} buckets, launched from post-accumulate hooks during backward",
+                          "exposed_ms_per_step": exposed_ms},
+            "ms_per_step_without_allreduce": solo_ms,
+            "efficiency_vs_1gpu": solo_ms / dp_ms,
+            "replica_param_checksum_rel_spread": spread, "final_loss": loss_val}
+
+
 def run_train_arm(args, cfg):
     import torch
     from tributary_b200.attention import device_status
-    from tributary_b200.encoder import RTEncoder
-    from tributary_b200.train import TrainStep, build_masks
+    from tributary_b200.train import build_masks
     world, rank, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
-    cells = make_train_cells(cfg, 1000 + rank)
-    host = {k: v.pin_memory() for k, v in cells_to_host_tensors(cells).items()}
-    d = {k: v.to(dev) for k, v in host.items()}
-    for k in ("target_stype", "cat_start"):
-        d[k] = cells[k]
-    col = torch.from_numpy(cells["col_table"]).to(dev)
-    cat = torch.from_numpy(cells["cat_table"]).to(dev)
-    torch.manual_seed(1234)  # identical initial weights on every rank
-    model = RTEncoder(encoder_config(cfg)).to(dev)
-    step = TrainStep(model)
-
-    def one_step():
-        return step(d, build_masks(d, TRAIN_KINDS), col, cat)
-
+    run = TrainRun(cfg, rank, dev)
     for _ in range(args.warmup):
-        one_step()
+        run()
     barrier(world)
     if device_status(reset=True) != 0:
         raise RuntimeError("device status error during warm-up")
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
+    step_ms, exposed_ms, loss = run.timed(args.steps, world, finish_events=True)
+    clocks = sampler.stop()
+    # end to end: every step copies its cell arrays from pinned host memory and reads the loss back
+    h2d = sum(v.numel() * v.element_size() for v in run.host.values())
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        loss = one_step()
-    e1.record()
-    barrier(world)
-    clocks = sampler.stop()
-    step_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
-    # end to end: every step copies its cell arrays from pinned host memory and reads the loss back
-    h2d = sum(v.numel() * v.element_size() for v in host.values())
-    barrier(world)
-    e0.record()
-    for _ in range(args.steps):
-        for k, v in host.items():
-            d[k].copy_(v, non_blocking=True)
-        loss_val = one_step().item()
+        for k, v in run.host.items():
+            run.d[k].copy_(v, non_blocking=True)
+        loss_val = run().item()
     e1.record()
     barrier(world)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
@@ -617,20 +754,11 @@ def run_train_arm(args, cfg):
     if status != 0 or not math.isfinite(loss_val):
         raise RuntimeError(f"device status {status}, loss {loss_val}")
     tokens = cfg["B"] * cfg["S"]
-    flops, attn_flops = train_flops(model, cfg, build_masks(d, TRAIN_KINDS), tokens)
-    # replicas must stay identical: same initial weights, same averaged gradients
-    with torch.no_grad():
-        chk = torch.stack([p.double().sum() for p in model.parameters()]).sum().reshape(1)
-    drift = 0.0
-    if world > 1:
-        import torch.distributed as dist
-        allc = [torch.zeros_like(chk) for _ in range(world)]
-        dist.all_gather(allc, chk)
-        vals = torch.cat(allc)
-        drift = float((vals.max() - vals.min()).abs() / vals.abs().max().clamp_min(1e-30))
+    flops, attn_flops = train_flops(run.model, cfg, build_masks(run.d, TRAIN_KINDS), tokens)
+    drift = run.checksum_spread(world)
     peak_tf, _, peak_src = measured_peaks()
     achieved = flops / (step_ms * 1e-3) / 1e12
-    n_params = sum(p.numel() for p in model.parameters())
+    n_params = sum(p.numel() for p in run.model.parameters())
     if rank == 0:
         line = {
             "metric": "rt_encoder_train_tokens_per_s", "value": world * tokens / (step_ms * 1e-3), "unit": "tokens/s",
@@ -642,7 +770,8 @@ def run_train_arm(args, cfg):
                        "optimizer": "muon (2-D weights) + adamw, global-norm clip 1.0",
                        "l2": "working set (activations of 48 sublayers) far above L2",
                        "parallelism": f"dp{world}: NCCL all-reduce (average) of fp32 gradients in "
-                                      f"{len(step.buckets.buffers)} buckets, overlapped with backward"},
+                                      f"{len(run.step.buckets.buffers)} buckets, overlapped with backward"},
+            "allreduce_exposed_ms_per_step": exposed_ms,
             "roofline": {"bound": "tensor", "kernel": "whole training step (matmuls + attention)",
                          "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
                          "peak_source": peak_src + " bf16 dense (burst)", "traffic": None,
@@ -763,6 +892,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-train", action="store_true",
+                    help="attention workloads: skip the data-parallel training-step record")
+    ap.add_argument("--train-steps", type=int, default=10,
+                    help="timed steps of the training-step record")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the workload's batch size (profiling runs)")
     args = ap.parse_args()

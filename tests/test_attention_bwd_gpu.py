@@ -4,7 +4,7 @@ forward): dq, dk, dv within 2e-2 max-relative."""
 import numpy as np
 import pytest
 
-from rt_cases import TOL_OUT, Case, from_bf16_tensor, max_rel
+from rt_cases import TOL_GRAD_ROW, TOL_OUT, Case, from_bf16_tensor, max_rel, per_head_errors, row_rel
 
 pytestmark = pytest.mark.gpu
 
@@ -36,6 +36,8 @@ def test_backward_matches_oracle(cuda_lib, gen, kind, dh):
         assert np.isfinite(g).all(), name
         err = max_rel(g, ref)
         assert err < TOL_OUT, (name, err)
+        err = row_rel(g, ref)
+        assert err < TOL_GRAD_ROW, (name, "row", err)
 
 
 def _same_up_to_dq_order(r1, r2):
@@ -114,13 +116,16 @@ def test_backward_repeated_under_concurrent_copies(cuda_lib):
     tile; every barrier phase must still be taken by each of its waiters before
     the next one completes. Repeat dense many-tile calls while a large copy runs
     on another stream (which shifts the timing) and require a clean device
-    status and identical dK / dV every time."""
+    status, identical dK / dV every time, and dQ within tolerance of the
+    float64 oracle head by head and row by row (a lost partial would move a
+    whole row)."""
     import torch
     from tributary_b200.attention import attention_bwd, attention_fwd, device_status
     c = Case((56, 2, 2048, 3, 4, 8, 0.7, 0.0), 3, h=4, dh=64, seed=11)
     o, lse = attention_fwd(c.qd, c.kd, c.vd, c.plan, c.scale)
     ref = attention_bwd(c.qd, c.kd, c.vd, o, lse, c.dod, c.plan, c.scale)
     assert device_status() == 0
+    dq_oracle = c.oracle_by_head()[2]
     side = torch.cuda.Stream()
     src = torch.empty(64 << 20, dtype=torch.uint8, device="cuda")
     host = torch.empty(64 << 20, dtype=torch.uint8).pin_memory()
@@ -134,10 +139,10 @@ def test_backward_repeated_under_concurrent_copies(cuda_lib):
         torch.cuda.synchronize()
         assert device_status() == 0, it
         assert torch.equal(dk, ref[1]) and torch.equal(dv, ref[2]), it
-        # dQ: reduction order moves an element by at most about one bf16 unit of
-        # its own size; a lost partial would move whole rows. (Element-wise
-        # relative error is no measure here: a million sums of 16 partials
-        # include elements that cancel to near zero.)
+        head_err, row_err = per_head_errors(from_bf16_tensor(dq), dq_oracle)
+        assert head_err < TOL_OUT and row_err < TOL_GRAD_ROW, (it, head_err, row_err)
+        # and against the first call: reduction order moves an element by at
+        # most about one bf16 unit of its own size
         err = max_rel(from_bf16_tensor(dq), from_bf16_tensor(ref[0]))
         assert err < 2.0 ** -7, (it, err)
 

@@ -5,7 +5,7 @@ import pytest
 
 from conftest import golden_files, load_golden, unpack_mask
 from oracle import rt_oracle as orc
-from rt_cases import TOL_LSE, TOL_OUT, Case, bf16_tensor, from_bf16_tensor, max_rel
+from rt_cases import TOL_LSE, TOL_OUT, Case, bf16_tensor, from_bf16_tensor, max_rel, row_rel
 
 pytestmark = pytest.mark.gpu
 
@@ -29,6 +29,7 @@ def test_forward_matches_oracle(cuda_lib, gen, kind, dh):
     o_got = from_bf16_tensor(o)
     assert np.isfinite(o_got).all()
     assert max_rel(o_got, o_ref) < TOL_OUT
+    assert row_rel(o_got, o_ref) < TOL_OUT
     np.testing.assert_allclose(lse.cpu().numpy(), lse_ref, atol=TOL_LSE, rtol=0)
 
 

@@ -4,8 +4,9 @@ Callers such as a plugin host or FFI handler with no scratch-allocation hook,
 or a service that may not call cudaMalloc after start-up, cannot hand
 rt_attention_bwd its workspace; this entry point keeps that workspace in a
 fixed array inside the library. These tests call it through the C ABI and
-compare it with rt_attention_bwd on the same inputs, for consecutive calls
-on different problems (the array keeps the previous call's contents).
+compare it with rt_attention_bwd on the same inputs and with the float64
+oracle's gradients, for consecutive calls on different problems (the array
+keeps the previous call's contents).
 
 The file name makes pytest collect it last.
 """
@@ -13,7 +14,7 @@ import ctypes
 
 import pytest
 
-from rt_cases import TOL_OUT, Case, from_bf16_tensor, max_rel
+from rt_cases import TOL_GRAD_ROW, TOL_OUT, Case, from_bf16_tensor, max_rel, row_rel
 
 pytestmark = pytest.mark.gpu
 
@@ -38,6 +39,7 @@ def test_noalloc_backward_matches_workspace_backward(cuda_lib):
         Case((62, 4, 256, 3, 4, 8, 0.6, 0.05), 3, h=2, dh=32, seed=72),
     ]
     cases.append(cases[0])  # a third call back on the first problem
+    oracle = {}
     for c in cases:
         o, lse = attention_fwd(c.qd, c.kd, c.vd, c.plan, c.scale)
         want = attention_bwd(c.qd, c.kd, c.vd, o, lse, c.dod, c.plan, c.scale)
@@ -45,8 +47,13 @@ def test_noalloc_backward_matches_workspace_backward(cuda_lib):
         _lib.check(st, "rt_attention_bwd_noalloc")
         torch.cuda.synchronize()
         assert device_status() == 0
-        for g, w in zip(got, want):
-            assert max_rel(from_bf16_tensor(g), from_bf16_tensor(w)) < TOL_OUT
+        if id(c) not in oracle:
+            oracle[id(c)] = c.oracle_bwd()
+        for name, g, w, r in zip(("dq", "dk", "dv"), got, want, oracle[id(c)]):
+            gv = from_bf16_tensor(g)
+            assert max_rel(gv, from_bf16_tensor(w)) < TOL_OUT, name
+            assert max_rel(gv, r) < TOL_OUT, name
+            assert row_rel(gv, r) < TOL_GRAD_ROW, name
 
 
 def test_noalloc_backward_rejects_problems_beyond_its_array(cuda_lib):

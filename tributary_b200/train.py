@@ -27,9 +27,14 @@ import torch.distributed as dist
 
 
 class GradBuckets:
-    def __init__(self, params, group=None, bucket_bytes: int = 32 << 20):
+    """Flat fp32 gradient buckets with overlapped all-reduce. ``reduce=False``
+    keeps the buckets but launches no collective (each rank steps on its own
+    gradients): the single-GPU step on the same device, for comparison."""
+
+    def __init__(self, params, group=None, bucket_bytes: int = 32 << 20, reduce: bool = True):
         self.group = group
-        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        joined = dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size(group) if joined and reduce else 1
         self.avg = self.world > 1 and dist.get_backend(group) == "nccl"  # NCCL averages in the reduction
         params = [p for p in params if p.requires_grad]
         groups, cur, size = [], [], 0
@@ -162,9 +167,12 @@ class TrainStep:
 
     def __init__(self, model, group=None, muon_lr: float = 0.02, adamw_lr: float = 3e-4,
                  weight_decay: float = 0.1, max_grad_norm: float = 1.0, bucket_bytes: int = 32 << 20,
-                 autocast: bool = True):
+                 autocast: bool = True, reduce: bool = True):
         self.model = model
-        self.buckets = GradBuckets(model.parameters(), group, bucket_bytes)
+        self.buckets = GradBuckets(model.parameters(), group, bucket_bytes, reduce=reduce)
+        # (start, end) CUDA events around finish() of each step while set: the
+        # all-reduce time the backward did not hide
+        self.finish_events = None
         mats = [p for p in model.parameters() if p.requires_grad and p.ndim == 2]
         rest = [p for p in model.parameters() if p.requires_grad and p.ndim != 2]
         dev = next(model.parameters()).device
@@ -180,7 +188,14 @@ class TrainStep:
             out = self.model(cells, masks, col_table, cat_table)
             loss = self.model.loss(out, cells, cat_table)
         loss.backward()
-        self.buckets.finish()
+        if self.finish_events is not None:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
+            self.buckets.finish()
+            ev[1].record()
+            self.finish_events.append(ev)
+        else:
+            self.buckets.finish()
         norm = self.buckets.global_norm()
         clip = torch.clamp(self.max_grad_norm / (norm + 1e-6), max=1.0)
         torch._foreach_mul_(self.buckets.buffers, clip)
