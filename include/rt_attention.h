@@ -193,12 +193,26 @@ int rt_attention_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, co
  * RT_ERR_WORKSPACE. All calls on a device share the array: calls that
  * overlap on the GPU race and must be ordered (one stream or events). The
  * first call on each device looks up the array's address and should come
- * before any stream capture. Allocates nothing. */
+ * before any stream capture; the address is kept for the process, so a
+ * cudaDeviceReset between calls is not supported. Allocates nothing. */
 int rt_attention_bwd_noalloc(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                              const uint16_t* o, const uint16_t* d_o, const float* lse,
                              int32_t batch, int32_t heads, int32_t seq_len, int32_t head_dim,
                              float scale, const rt_tile_plan* plan, uint16_t* dq, uint16_t* dk,
                              uint16_t* dv, void* stream);
+
+/* Diagnostic for the failure path (no counterpart in the reference, which has
+ * no device code). Launches one block that allocates tensor memory and waits
+ * on an mbarrier nothing arrives at, through the bounded wait every kernel
+ * here uses, with a limit of `limit_cycles` SM clocks (0 < limit_cycles <=
+ * the kernels' own limit, about one second). The wait runs out, the block's
+ * other waits leave through its abort flag, tensor memory is freed and the
+ * kernel returns; rt_device_status() then reports RT_ERR_TIMEOUT and the
+ * context stays usable. `report` (4 int32, device memory) receives: the
+ * abort flag, the number of waits that gave up (3 expected), and the SM
+ * clocks in millions that the running-out wait and the longest other wait
+ * took. No fault, trap or hang is involved. */
+int rt_selftest_bounded_wait(int64_t limit_cycles, int32_t* report, void* stream);
 
 /* Sticky device status (RT_OK or RT_ERR_TIMEOUT) raised by any kernel of the
  * library on the current device. Synchronises the device. If `reset` is

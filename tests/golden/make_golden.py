@@ -3,7 +3,7 @@
 Run in the build container (it reads the reference checkout, which does not
 exist where the GPU tests run):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <path of the reference checkout>
 
 jax, flax and optax are not installable here, so the reference modules are
 imported over a small numpy stand-in (``_NumpyJax`` / ``_MiniFlax`` below)
@@ -376,7 +376,8 @@ def make_sublayer_fixture(config, layers, model, bt, h, dh, kind, seed):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="root of the reference checkout (holds confluence/ and documentation/)")
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
     config, layers, model = load_reference(args.reference)

@@ -1,7 +1,7 @@
 """ctypes binding of libtributary_b200.so (the C ABI in include/rt_attention.h).
 
-This is the same binding a reference-side integration writes (see
-INTEGRATION.md); the Python host layer in ``tributary_b200.attention`` and the
+This is the same binding a reference-side integration writes; the Python
+host layer in ``tributary_b200.attention`` and the
 tests call the library through it. There is no fallback: if the shared
 library is missing or fails to load, ``load()`` raises.
 """
@@ -33,6 +33,7 @@ EXPORTED = (
     "rt_attention_bwd_noalloc", "rt_column_order", "rt_rcm_order",
     "rt_qk_prepare", "rt_qk_prepare_bwd", "rt_heads_unpermute", "rt_heads_permute",
     "rt_device_status", "rt_status_string", "rt_last_error", "rt_version",
+    "rt_selftest_bounded_wait",
 )
 
 
@@ -104,6 +105,8 @@ def _declare(lib):
     lib.rt_last_error.restype = ctypes.c_char_p
     lib.rt_version.argtypes = []
     lib.rt_version.restype = i32
+    lib.rt_selftest_bounded_wait.argtypes = [ctypes.c_int64, vp, vp]
+    lib.rt_selftest_bounded_wait.restype = ctypes.c_int
 
 
 def load(path: str | None = None):

@@ -58,9 +58,10 @@ def build(force: bool = False, verbose: bool = False) -> str:
     log = proc.stdout + proc.stderr
     if proc.returncode != 0:
         raise RuntimeError(f"nvcc failed ({proc.returncode}):\n{log}")
-    # registers, spills and shared memory per kernel; compile times are left
-    # out so the file changes only when the code generation does
-    with open(os.path.join(PKG, "build_ptxas.log"), "w") as f:
+    # registers, spills and shared memory per kernel (build output, kept out of
+    # the package and of version control); compile times are left out
+    os.makedirs(os.path.join(REPO, "_build"), exist_ok=True)
+    with open(os.path.join(REPO, "_build", "ptxas.log"), "w") as f:
         f.write("".join(l for l in log.splitlines(keepends=True) if "Compile time" not in l))
     if verbose:
         print(log)

@@ -214,15 +214,19 @@ struct EpiSlice {
 // negated so they enter the exponent / difference as FMA addends:
 //   stats[bh][0][q] = -lse[bh][q] * log2(e)                 (0 for q >= S)
 //   stats[bh][1][q] = -sum_d dO[bh][q][d] * O[bh][q][d]     (0 for q >= S)
-// and, when aux is given, the fused kernel's operand row per padded query:
+// when stats is given (the two-kernel path), and, when aux is given, the fused
+// kernel's operand row per padded query:
 //   aux[bh * Sp + q] = bf16 (a_hi, a_lo, d_hi, d_lo, 0 x 12),
-//   a = -lse / scale, d = stats[bh][1][q], x_hi = bf16(x), x_lo = bf16(x - x_hi).
+//   a = -lse / scale, d = -sum_d dO O, x_hi = bf16(x), x_lo = bf16(x - x_hi),
+// and, when dq_acc is given, zeroes the fused kernel's fp32 dQ accumulator
+// dq_acc [bh * Sp + q][DH] (each thread clears the 8 columns it reads).
 template <int DH>
 __global__ void __launch_bounds__(256) row_stats_kernel(const uint16_t* __restrict__ o,
                                                         const uint16_t* __restrict__ d_o,
                                                         const float* __restrict__ lse,
                                                         float* __restrict__ stats, uint16_t* __restrict__ aux,
-                                                        float inv_scale, int S, int Sp, long long rows_padded) {
+                                                        float* __restrict__ dq_acc, float inv_scale, int S, int Sp,
+                                                        long long rows_padded) {
   constexpr int kLanesPerRow = DH / 8;
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long prow = gid / kLanesPerRow;
@@ -247,11 +251,18 @@ __global__ void __launch_bounds__(256) row_stats_kernel(const uint16_t* __restri
   }
 #pragma unroll
   for (int off = kLanesPerRow / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, off);
+  if (dq_acc != nullptr && prow < rows_padded) {
+    float4* z = reinterpret_cast<float4*>(dq_acc + prow * DH + sub * 8);
+    z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   if (prow < rows_padded && sub == 0) {
     const float l = in ? lse[bh * S + q] : 0.f;
-    float* st = stats + bh * 2 * Sp;
-    st[q] = in ? -l * 1.4426950408889634f : 0.f;
-    st[Sp + q] = -acc;
+    if (stats != nullptr) {
+      float* st = stats + bh * 2 * Sp;
+      st[q] = in ? -l * 1.4426950408889634f : 0.f;
+      st[Sp + q] = -acc;
+    }
     if (aux != nullptr) {
       const float a = -l * inv_scale, d = -acc;
       const float a_hi = __bfloat162float(__float2bfloat16_rn(a));
@@ -1080,14 +1091,14 @@ int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16
   const long long threads = rows_padded * (DH / 8);
   // fused path: the statistics ride in the MMAs as -lse / scale, so scale > 0
   const bool fused = dq_acc != nullptr && aux != nullptr && scale > 0.f && scale < 3.0e38f;
+  // fused path: operand rows and the zeroed dQ accumulator; otherwise the statistics
   row_stats_kernel<DH><<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
-      o, d_o, lse, stats, fused ? aux : nullptr, fused ? 1.0f / scale : 0.f, S, Sp, rows_padded);
+      o, d_o, lse, fused ? nullptr : stats, fused ? aux : nullptr, fused ? dq_acc : nullptr,
+      fused ? 1.0f / scale : 0.f, S, Sp, rows_padded);
   if (int st = check_launch("row_stats_kernel launch")) return st;
   const float scale_log2 = scale * 1.4426950408889634f;
   dim3 grid(plan.tiles, H, B);
   if (fused) {  // one pass for dK, dV and dQ
-    cudaError_t e = cudaMemsetAsync(dq_acc, 0, sizeof(float) * (size_t)rows_padded * DH, stream);
-    if (e != cudaSuccess) return cuda_failure(e, "cudaMemsetAsync(dq accumulator)");
     CUtensorMap tacc, taux;
     if (make_acc_tensor_map(&tacc, dq_acc, rows_padded, DH) != RT_OK) return RT_ERR_CUDA;
     if (make_aux_tensor_map(&taux, aux, rows_padded) != RT_OK) return RT_ERR_CUDA;

@@ -92,20 +92,27 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
   return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete. Returns false
-// (and leaves the abort flag set) if the block is aborting or the wait ran out.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+// Bounded wait for the phase with the given parity to complete, giving up
+// after limit_cycles SM clocks. Returns false (and leaves the abort flag set)
+// if the block is aborting or the wait ran out.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                long long limit_cycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   for (;;) {
     if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > RT_WAIT_CYCLES) {
+    if (clock64() - t0 > limit_cycles) {
       *abort_flag = 1;
       raise_status(RT_ERR_TIMEOUT);
       return false;
     }
   }
+}
+
+// The kernels' bounded wait: limit RT_WAIT_CYCLES.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  return mbar_wait_limit(bar, parity, abort_flag, RT_WAIT_CYCLES);
 }
 
 // mbar_wait for code that the whole warp runs together: every lane gets the

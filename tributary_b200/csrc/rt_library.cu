@@ -9,3 +9,4 @@
 #include "token_prep.cu"
 #include "attn_bwd_noalloc.cu"
 #include "row_order.cu"
+#include "selftest.cu"

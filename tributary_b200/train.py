@@ -20,10 +20,63 @@ clipping the global gradient norm (config.py:64).
 """
 from __future__ import annotations
 
+import datetime
 import math
 
 import torch
 import torch.distributed as dist
+
+
+class RankFailure(RuntimeError):
+    """A rank did not reach a training step within the heartbeat deadline (it
+    left, crashed or stalled), or a gradient all-reduce failed or ran past its
+    deadline. The process group has been aborted when this is raised, so no
+    rank is left waiting in a collective."""
+
+
+class Heartbeat:
+    """Per-step liveness of the data-parallel ranks through the process
+    group's key-value store (documentation/system_architecture.md:747 asks
+    for failure detection around the gradient exchange).
+
+    step(n) records that this rank reached step n, then waits until every rank
+    has, before any collective of step n is launched. A rank that left between
+    steps therefore surfaces on the host as RankFailure (naming the missing
+    ranks) within `timeout_s`, instead of as a collective that never
+    completes."""
+
+    def __init__(self, group=None, store=None, timeout_s: float = 60.0, prefix: str = "rt_train_hb"):
+        self.group = group
+        self.store = store if store is not None else dist.distributed_c10d._get_default_store()
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.timeout = datetime.timedelta(seconds=timeout_s)
+        self.prefix = prefix
+
+    def _key(self, step, rank):
+        return f"{self.prefix}/{step}/{rank}"
+
+    def step(self, n: int):
+        self.store.set(self._key(n, self.rank), "1")
+        keys = [self._key(n, r) for r in range(self.world)]
+        try:
+            self.store.wait(keys, self.timeout)
+        except Exception as e:  # the store raises on its deadline
+            missing = [r for r, k in enumerate(keys) if not self.store.check([k])]
+            abort(self.group)
+            raise RankFailure(f"step {n}: rank(s) {missing} did not arrive within "
+                              f"{self.timeout.total_seconds():g} s") from e
+        if n >= 2:  # every rank has passed step n - 1, so nobody reads step n - 2 any more
+            self.store.delete_key(self._key(n - 2, self.rank))
+
+
+def abort(group=None):
+    """Abort the process group (pending collectives end with an error on every
+    rank instead of waiting for the missing one)."""
+    try:
+        dist.distributed_c10d._abort_process_group(group)
+    except Exception:  # already aborted or destroyed
+        pass
 
 
 class GradBuckets:
@@ -62,6 +115,7 @@ class GradBuckets:
             self.views.append(views)
         self.pending = [len(g) for g in groups]
         self.works = []
+        self.launch_error = None
         self.launched = [False] * len(groups)
 
     @property
@@ -86,7 +140,10 @@ class GradBuckets:
         self.launched[i] = True
         if self.world > 1:
             op = dist.ReduceOp.AVG if self.avg else dist.ReduceOp.SUM
-            self.works.append(dist.all_reduce(self.buffers[i], op=op, group=self.group, async_op=True))
+            try:
+                self.works.append(dist.all_reduce(self.buffers[i], op=op, group=self.group, async_op=True))
+            except Exception as e:  # raised from a backward hook: report it from finish()
+                self.launch_error = e
 
     def zero(self):
         """Clear the buckets before a backward pass."""
@@ -98,15 +155,31 @@ class GradBuckets:
         self.pending = [len(g) for g in self.params]
         self.launched = [False] * len(self.params)
         self.works = []
+        self.launch_error = None
 
-    def finish(self):
+    def finish(self, timeout_s: float | None = None):
         """Reduce the buckets no hook completed (parameters without a
         gradient this step), wait for every all-reduce, and turn sums into
-        means where the backend cannot average."""
+        means where the backend cannot average. With `timeout_s`, an
+        all-reduce that fails or does not complete in time aborts the process
+        group and raises RankFailure. (NCCL's wait only orders the current
+        stream behind the collective; its deadline is the process group's
+        timeout, and the heartbeat catches ranks that left between steps.)"""
         for i in range(len(self.buffers)):
             self._launch(i)
-        for w in self.works:
-            w.wait()
+        try:
+            if self.launch_error is not None:
+                raise self.launch_error
+            for w in self.works:
+                if timeout_s is None:
+                    w.wait()
+                else:
+                    w.wait(timeout=datetime.timedelta(seconds=timeout_s))
+        except Exception as e:
+            self.works = []
+            self.launch_error = None
+            abort(self.group)
+            raise RankFailure(f"gradient all-reduce failed: {e}") from e
         self.works = []
         if self.world > 1 and not self.avg:
             for buf in self.buffers:
@@ -167,8 +240,12 @@ class TrainStep:
 
     def __init__(self, model, group=None, muon_lr: float = 0.02, adamw_lr: float = 3e-4,
                  weight_decay: float = 0.1, max_grad_norm: float = 1.0, bucket_bytes: int = 32 << 20,
-                 autocast: bool = True, reduce: bool = True):
+                 autocast: bool = True, reduce: bool = True, heartbeat: Heartbeat | None = None,
+                 allreduce_timeout_s: float | None = None):
         self.model = model
+        self.heartbeat = heartbeat
+        self.allreduce_timeout_s = allreduce_timeout_s
+        self.steps = 0
         self.buckets = GradBuckets(model.parameters(), group, bucket_bytes, reduce=reduce)
         # (start, end) CUDA events around finish() of each step while set: the
         # all-reduce time the backward did not hide
@@ -183,6 +260,9 @@ class TrainStep:
         self.autocast = autocast and dev.type == "cuda"
 
     def __call__(self, cells, masks, col_table, cat_table) -> torch.Tensor:
+        if self.heartbeat is not None:  # every rank is here before any collective of this step
+            self.heartbeat.step(self.steps)
+        self.steps += 1
         self.buckets.zero()
         with torch.autocast("cuda", dtype=torch.bfloat16, enabled=self.autocast):
             out = self.model(cells, masks, col_table, cat_table)
@@ -191,11 +271,11 @@ class TrainStep:
         if self.finish_events is not None:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             ev[0].record()
-            self.buckets.finish()
+            self.buckets.finish(self.allreduce_timeout_s)
             ev[1].record()
             self.finish_events.append(ev)
         else:
-            self.buckets.finish()
+            self.buckets.finish(self.allreduce_timeout_s)
         norm = self.buckets.global_norm()
         clip = torch.clamp(self.max_grad_norm / (norm + 1e-6), max=1.0)
         torch._foreach_mul_(self.buckets.buffers, clip)
