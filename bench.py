@@ -299,6 +299,156 @@ class Workload:
         return {"fwd": 4 * fwd, "bwd": 4 * bwd}
 
 
+# ----------------------------------------------------------------------------
+# sub-records of the default line: the B=32, S=1024, Dh=32 workload and the
+# sequence-length x density sweep (8 heads x 64)
+# ----------------------------------------------------------------------------
+SWEEP_S = (512, 1024, 2048, 4096, 8192)
+SWEEP_TARGETS = (0.01, 0.05, 0.20, 0.50, 1.00)
+SWEEP_TOKENS = 1 << 18  # B * S per point: q, k, v, dO are 256 MB each, above L2
+# generator settings the sweep picks from (tables, cells_lo, cells_hi, p_fk,
+# max_parents, parent_window), from sparse to dense live tiles; with the four
+# mask kinds they span about 5-50% at S = 4096 (and 100%: full kind, no padding)
+SWEEP_SETTINGS = (
+    (96, 16, 32, 0.3, 1, 8),
+    (96, 8, 24, 0.3, 1, 32),
+    (24, 2, 6, 0.5, 2, 128),
+    (24, 4, 16, 0.9, 2, None),
+    (48, 1, 3, 0.9, 6, None),
+    (96, 2, 6, 1.0, 6, None),
+)
+
+
+def _sweep_batch(seed, b, s, setting, pad):
+    from tributary_b200 import batch as rb
+    t, lo, hi, p, mp, win = setting
+    return rb.make_batch(seed, b, s, t, lo, hi, p, pad, parent_window=win, max_parents=mp)
+
+
+def _plan_for(bt, kind, device):
+    import torch
+    from tributary_b200 import attention as rt
+    from tributary_b200 import batch as rb
+    dev = {k: torch.from_numpy(np.ascontiguousarray(v).view(np.int16) if v.dtype == np.uint16 else
+                               np.ascontiguousarray(v)).to(device)
+           for k, v in bt.items() if k in ("seq_row_ids", "column_ids", "is_padding", "fk_adj")}
+    perm = torch.from_numpy(np.ascontiguousarray(rb.order_for_kind(bt, kind)).view(np.int16)).to(device)
+    return rt.build_tile_plan(perm, dev["seq_row_ids"], dev["column_ids"], dev["is_padding"], dev["fk_adj"],
+                              kind), (perm, dev)
+
+
+def sweep_choices(s, device):
+    """(target, setting, kind, calibration density) per density target at
+    sequence length s: the generator setting and mask kind whose live-tile
+    density on a 2-sample calibration batch is nearest the target (log
+    scale). The seed does not depend on the rank, so every rank picks alike."""
+    cands = [(1.0, None, 3)]
+    for setting in SWEEP_SETTINGS:
+        bt = _sweep_batch(77, 2, s, setting, 0.05)
+        for kind in (0, 1, 2):
+            plan, _ = _plan_for(bt, kind, device)
+            t = plan.tiles
+            cands.append((plan.nnz() / (2 * t * t), setting, kind))
+    out = []
+    for target in SWEEP_TARGETS:
+        d, setting, kind = min(cands, key=lambda c: abs(math.log(c[0] / target)))
+        out.append((target, setting, kind, d))
+    return out
+
+
+def sweep_point(s, setting, kind, seed, device, world, steps=5, warmup=2, h=8, dh=64):
+    """fwd + bwd of one mask kind at sequence length s on SWEEP_TOKENS cells,
+    device-resident inputs; times are CUDA events, max over ranks."""
+    import torch
+    from tributary_b200 import attention as rt
+    b = SWEEP_TOKENS // s
+    bt = _sweep_batch(seed, b, s, setting if setting is not None else SWEEP_SETTINGS[0],
+                      0.0 if kind == 3 else 0.05)
+    plan, (perm, dev) = _plan_for(bt, kind, device)
+    g = torch.Generator(device=device).manual_seed(seed)
+    q = torch.randn(b, h, s, dh, device=device, generator=g)
+    k = torch.randn(b, h, s, dh, device=device, generator=g)
+    q = (q / q.norm(dim=-1, keepdim=True) * math.sqrt(dh)).to(torch.bfloat16)
+    k = (k / k.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    v = torch.randn(b, h, s, dh, device=device, generator=g).to(torch.bfloat16)
+    do = torch.randn(b, h, s, dh, device=device, generator=g).to(torch.bfloat16)
+    o, lse = torch.empty_like(q), torch.empty(b, h, s, dtype=torch.float32, device=device)
+    grads = [torch.empty_like(q) for _ in range(3)]
+    ws = torch.empty(rt._lib.load().rt_attention_bwd_workspace_bytes(b, h, s), dtype=torch.uint8, device=device)
+    scale = 1.0 / math.sqrt(dh)
+
+    def call():
+        rt.attention_fwd(q, k, v, plan, scale, out=o, lse=lse)
+        rt.attention_bwd(q, k, v, o, lse, do, plan, scale, dq=grads[0], dk=grads[1], dv=grads[2], workspace=ws)
+
+    for _ in range(warmup):
+        call()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        call()
+    e1.record()
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    nnz, t = plan.nnz(), plan.tiles
+    tflops = 14 * 128 * 128 * dh * h * nnz / (ms * 1e-3) / 1e12
+    return {"S": s, "B": b, "kind": KIND_NAMES[kind], "live_tile_density": nnz / (b * t * t),
+            "ms_fwd_bwd": ms, "cells_per_s": world * b * s / (ms * 1e-3), "tflops_live_tiles": tflops}
+
+
+def run_sweep(world, rank, device, peak_tf):
+    import torch
+    points = []
+    for s in SWEEP_S:
+        for target, setting, kind, _ in sweep_choices(s, device):
+            rec = sweep_point(s, setting, kind, 2000 + rank, device, world)
+            rec["target_density"] = target
+            rec["generator"] = None if setting is None else dict(zip(
+                ("tables", "cells_lo", "cells_hi", "p_fk", "max_parents", "parent_window"), setting))
+            rec["frac_of_bf16_peak"] = rec["tflops_live_tiles"] / peak_tf
+            points.append(rec)
+            torch.cuda.empty_cache()
+    return {"what": "fwd+bwd of one mask kind, H=8, Dh=64, B*S = %d cells per point (inputs > L2), "
+                    "generator setting and kind chosen per point for the live-tile density nearest the "
+                    "target (the diagonal tiles alone are 1/T, so 1%% is out of reach below S = 12800)"
+                    % SWEEP_TOKENS,
+            "points": points}
+
+
+def measure_workload(cfg, seed, device, world, steps=5, warmup=3):
+    """Device time of the attention step (prepass, fwd, bwd of the four kinds)
+    on cfg's workload, with the per-kind breakdown; max over ranks."""
+    import torch
+    wl = Workload(cfg, seed=seed, device=device)
+    for _ in range(warmup):
+        wl.step()
+    barrier(world)
+    ev = {n: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for n in ("plan", "fwd", "bwd")}
+    ev["acc"] = {"plan": [], "fwd": [], "bwd": []}
+    ev["by_kind"] = {}
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        wl.step(events=ev)
+    e1.record()
+    barrier(world)
+    step_ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    kind_ms = {KIND_NAMES[kk]: {n: max_over_ranks(sum(a.elapsed_time(b) for a, b in ev["by_kind"][(kk, n)]) / steps,
+                                                  world) for n in ("plan", "fwd", "bwd")} for kk in range(4)}
+    flops = wl.live_tile_flops()
+    attn_ms = sum(v["fwd"] + v["bwd"] for v in kind_ms.values())
+    tf = (flops["fwd"] + flops["bwd"]) / (attn_ms * 1e-3) / 1e12
+    densities = {KIND_NAMES[i]: wl.nnz[i] / (cfg["B"] * wl.tiles * wl.tiles) for i in range(4)}
+    rec = {"workload": cfg["name"], "B": cfg["B"], "S": cfg["S"], "H": cfg["H"], "Dh": cfg["Dh"],
+           "ms_per_step": step_ms, "cells_per_s": world * 4 * cfg["B"] * cfg["S"] / (step_ms * 1e-3),
+           "breakdown_ms_by_kind": kind_ms, "live_tile_density": densities, "tflops_live_tiles": tf}
+    del wl
+    torch.cuda.empty_cache()
+    return rec
+
+
 def dist_setup(n_gpus):
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -531,6 +681,12 @@ def run_our_arm(args, cfg):
     densities = {KIND_NAMES[i]: wl.nnz[i] / (cfgd["B"] * wl.tiles * wl.tiles) for i in range(4)}
     del wl
     torch.cuda.empty_cache()
+    sweep = config_b = None
+    if not args.no_sweep:
+        dev = torch.device("cuda", local)
+        config_b = measure_workload(dict(CONFIGS["b"]), 1000 + rank, dev, world)
+        config_b["frac_of_bf16_peak"] = config_b["tflops_live_tiles"] / peak_tf
+        sweep = run_sweep(world, rank, dev, peak_tf)
     train = None
     if not args.no_train:
         train = measure_train(dict(CONFIGS["d"]), args.train_steps, 3, world, rank, local)
@@ -563,6 +719,9 @@ def run_our_arm(args, cfg):
             "gpu_launches": launches,
             "clocks": clocks,
         }
+        if config_b is not None:
+            line["config_b"] = config_b
+            line["sweep"] = sweep
         if train is not None:
             line["train_step"] = train
         if not args.no_cpu_baseline:
@@ -894,6 +1053,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-train", action="store_true",
                     help="attention workloads: skip the data-parallel training-step record")
+    ap.add_argument("--no-sweep", action="store_true",
+                    help="attention workloads: skip the B=32 S=1024 record and the length x density sweep")
     ap.add_argument("--train-steps", type=int, default=10,
                     help="timed steps of the training-step record")
     ap.add_argument("--batch", type=int, default=None,
