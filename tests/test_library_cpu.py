@@ -100,3 +100,13 @@ def test_argument_validation_before_device_work(lib):
     assert lib.rt_attention_bwd(fake, fake, fake, fake, fake, fake, 1, 1, 128, 64, 1.0,
                                 ctypes.byref(plan), fake, fake, fake, fake, ws - 256,
                                 None) == _lib.RT_ERR_WORKSPACE
+
+
+def test_xla_ffi_handlers_need_jax():
+    """The XLA FFI adapter builds only against jax's FFI headers; without jax
+    the build says so and returns None instead of failing."""
+    import importlib.util
+    from tributary_b200.ffi import build_ffi
+    assert os.path.exists(os.path.join(REPO, "tributary_b200", "ffi", "rt_xla_ffi.cc"))
+    if importlib.util.find_spec("jax") is None:
+        assert build_ffi.build() is None
