@@ -738,7 +738,7 @@ def run_our_arm(args, cfg):
 # full encoder training step (config d): data-parallel, NCCL gradient all-reduce
 # ----------------------------------------------------------------------------
 TRAIN_KINDS = (0, 1, 2, 3)
-CELL_ARRAYS = ("seq_row_ids", "column_ids", "is_padding", "fk_adj", "col_perm", "out_perm", "in_perm", "stypes",
+CELL_ARRAYS = ("seq_row_ids", "column_ids", "is_padding", "fk_adj", "out_perm", "in_perm", "stypes",
                "numeric_values", "timestamp_values", "bool_values", "categorical_ids", "text_ids", "text_vectors",
                "is_null", "is_target")
 
@@ -954,8 +954,9 @@ def run_train_arm(args, cfg):
 
 class _CpuOps:
     """The sublayer's gather, QK normalisation, dense masked attention and
-    scatter in plain torch with the reference's semantics (layers.py:63-97,
-    139-167), for the CPU baseline."""
+    scatter, and the layer's norms, gated residual and SwiGLU activation, in
+    plain torch with the reference's semantics (layers.py:16-30, 63-97,
+    139-174, 177-200), for the CPU baseline."""
 
     @staticmethod
     def qk_prepare(qkv, order, tau, heads, head_dim):
@@ -981,6 +982,26 @@ class _CpuOps:
         o = o.permute(0, 2, 1, 3).reshape(b, s, h * dh)
         inv = torch.empty_like(order).scatter_(1, order, torch.arange(s).expand_as(order))
         return torch.gather(o, 1, inv[:, :, None].expand(b, s, h * dh))
+
+    @staticmethod
+    def rms_norm(x, gamma, eps):
+        import torch.nn.functional as F
+        return F.rms_norm(x.float(), (x.shape[-1],), 1.0 + gamma, eps)
+
+    @staticmethod
+    def gate_residual(x, out, gate, scale):
+        import torch
+        return x + (out * scale * torch.sigmoid(gate)).float()
+
+    @staticmethod
+    def swiglu(u):
+        import torch.nn.functional as F
+        f = u.shape[-1] // 2
+        return F.silu(u[..., :f]) * u[..., f:]
+
+    @staticmethod
+    def residual_add(x, h, scale):
+        return x + (h * scale).float()
 
 
 def train_cpu_sample(cfg, budget_s):

@@ -114,6 +114,13 @@ int rt_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids,
 int rt_column_order(const int32_t* column_ids, const uint8_t* is_padding, int32_t batch,
                     int32_t seq_len, uint16_t* perm);
 
+/* rt_column_order on the GPU (device memory, stream-ordered): the same order,
+ * bit for bit, for seq_len <= 16384 (RT_ERR_UNSUPPORTED beyond), so that a
+ * batch in device memory reaches rt_build_tile_plan without a host round
+ * trip. Replaces headwater/src/sampler.rs:655-668 on the device. */
+int rt_column_order_device(const int32_t* column_ids, const uint8_t* is_padding, int32_t batch,
+                           int32_t seq_len, uint16_t* perm, void* stream);
+
 /* rt_rcm_order replaces headwater/src/sampler.rs:672-784: a reverse
  * Cuthill-McKee order of each sample's rows over its FK graph (fk_adj[i][j]
  * for outbound, fk_adj[j][i] for inbound), then cells sorted by (padding last,
@@ -200,6 +207,45 @@ int rt_attention_bwd_noalloc(const uint16_t* q, const uint16_t* k, const uint16_
                              int32_t batch, int32_t heads, int32_t seq_len, int32_t head_dim,
                              float scale, const rt_tile_plan* plan, uint16_t* dq, uint16_t* dk,
                              uint16_t* dv, void* stream);
+
+/* Fused kernels of the encoder layer around the attention sublayers (the
+ * data-parallel training step's non-attention work; device memory,
+ * stream-ordered, 16-byte aligned, widths multiples of 8).
+ *
+ * rt_rms_norm: ZeroCenteredRMSNorm (confluence/confluence/layers.py:16-30),
+ *   y = bf16(x / sqrt(mean(x^2) + eps) * (1 + gamma)); x fp32 [rows][d]
+ *   (d <= 1024), gamma fp32 [d], y bf16 [rows][d], rstd fp32 [rows] (kept
+ *   for the backward).
+ * rt_rms_norm_bwd: dx fp32 [rows][d] and dgamma fp32 [d] (summed in a fixed
+ *   order: deterministic) from dy bf16 [rows][d]; workspace of
+ *   rt_rms_norm_bwd_workspace_bytes(rows, d) bytes. */
+int rt_rms_norm(const float* x, const float* gamma, int64_t rows, int32_t d, float eps, uint16_t* y,
+                float* rstd, void* stream);
+size_t rt_rms_norm_bwd_workspace_bytes(int64_t rows, int32_t d);
+int rt_rms_norm_bwd(const uint16_t* dy, const float* x, const float* gamma, const float* rstd,
+                    int64_t rows, int32_t d, float* dx, float* dgamma, void* workspace,
+                    size_t workspace_bytes, void* stream);
+/* rt_gate_residual: the gated residual of GatedAttentionSublayer
+ *   (layers.py:170-174), y = x + scale * o * sigmoid(gate); x, y fp32 [n],
+ *   o (the W_O output) and gate (the W_gate output) bf16 [n].
+ * rt_gate_residual_bwd: d_o = bf16(dy scale s), d_gate = bf16(dy scale o s (1 - s)),
+ *   s = sigmoid(gate); dy fp32 [n] (the gradient of x is dy itself). */
+int rt_gate_residual(const float* x, const uint16_t* o, const uint16_t* gate, int64_t n, float scale,
+                     float* y, void* stream);
+int rt_gate_residual_bwd(const float* dy, const uint16_t* o, const uint16_t* gate, int64_t n,
+                         float scale, uint16_t* d_o, uint16_t* d_gate, void* stream);
+/* rt_residual_add: y = x + scale * h (the FFN's residual, layers.py:233-236);
+ *   x, y fp32 [n], h bf16 [n] (the W_down output).
+ * rt_residual_add_bwd: dh = bf16(dy scale) (the gradient of x is dy). */
+int rt_residual_add(const float* x, const uint16_t* h, int64_t n, float scale, float* y, void* stream);
+int rt_residual_add_bwd(const float* dy, int64_t n, float scale, uint16_t* dh, void* stream);
+/* rt_swiglu: the SwiGLU activation (layers.py:177-200) on the fused gate/up
+ *   projection u bf16 [rows][2f] (gate in columns [0, f), up in [f, 2f)):
+ *   h = bf16(silu(u[:, :f]) * u[:, f:]) [rows][f].
+ * rt_swiglu_bwd: du bf16 [rows][2f] = [dh up silu'(gate) | dh silu(gate)]. */
+int rt_swiglu(const uint16_t* u, int64_t rows, int32_t f, uint16_t* h, void* stream);
+int rt_swiglu_bwd(const uint16_t* dh, const uint16_t* u, int64_t rows, int32_t f, uint16_t* du,
+                  void* stream);
 
 /* Diagnostic for the failure path (no counterpart in the reference, which has
  * no device code). Launches one block that allocates tensor memory and waits

@@ -4,6 +4,7 @@ masks from the oracle, and batch conversion. Used as the encoder's attention
 in CPU tests (gloo ranks) and as the comparison in the GPU tests."""
 import numpy as np
 import torch
+import torch.nn.functional as F
 
 from oracle import rt_oracle as orc
 from tributary_b200 import batch as rb
@@ -48,6 +49,28 @@ class RefOps:
         o = o.permute(0, 2, 1, 3).reshape(b, s, h * dh)
         inv = inverse_order(order)
         return torch.gather(o, 1, inv[:, :, None].expand(b, s, h * dh))
+
+    # the layer norm, gated residual and SwiGLU activation in plain torch
+    # (layers.py:16-30, 170-174, 177-200)
+    @staticmethod
+    def rms_norm(x, gamma, eps):
+        y = F.rms_norm(x.float(), (x.shape[-1],), 1.0 + gamma, eps)
+        if torch.is_autocast_enabled(x.device.type):  # the output only feeds matmuls
+            y = y.to(torch.get_autocast_dtype(x.device.type))
+        return y
+
+    @staticmethod
+    def gate_residual(x, out, gate, scale):
+        return x + (out * scale * torch.sigmoid(gate)).float()
+
+    @staticmethod
+    def swiglu(u):
+        f = u.shape[-1] // 2
+        return F.silu(u[..., :f]) * u[..., f:]
+
+    @staticmethod
+    def residual_add(x, h, scale):
+        return x + (h * scale).float()
 
 
 def tiny_config(**kw):

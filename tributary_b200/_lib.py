@@ -33,7 +33,9 @@ EXPORTED = (
     "rt_attention_bwd_noalloc", "rt_column_order", "rt_rcm_order",
     "rt_qk_prepare", "rt_qk_prepare_bwd", "rt_heads_unpermute", "rt_heads_permute",
     "rt_device_status", "rt_status_string", "rt_last_error", "rt_version",
-    "rt_selftest_bounded_wait",
+    "rt_selftest_bounded_wait", "rt_column_order_device",
+    "rt_rms_norm", "rt_rms_norm_bwd_workspace_bytes", "rt_rms_norm_bwd", "rt_gate_residual",
+    "rt_gate_residual_bwd", "rt_swiglu", "rt_swiglu_bwd", "rt_residual_add", "rt_residual_add_bwd",
 )
 
 
@@ -105,6 +107,27 @@ def _declare(lib):
     lib.rt_last_error.restype = ctypes.c_char_p
     lib.rt_version.argtypes = []
     lib.rt_version.restype = i32
+    i64 = ctypes.c_int64
+    lib.rt_rms_norm.argtypes = [vp, vp, i64, i32, f32, vp, vp, vp]
+    lib.rt_rms_norm.restype = ctypes.c_int
+    lib.rt_rms_norm_bwd_workspace_bytes.argtypes = [i64, i32]
+    lib.rt_rms_norm_bwd_workspace_bytes.restype = sz
+    lib.rt_rms_norm_bwd.argtypes = [vp, vp, vp, vp, i64, i32, vp, vp, vp, sz, vp]
+    lib.rt_rms_norm_bwd.restype = ctypes.c_int
+    lib.rt_gate_residual.argtypes = [vp, vp, vp, i64, f32, vp, vp]
+    lib.rt_gate_residual.restype = ctypes.c_int
+    lib.rt_gate_residual_bwd.argtypes = [vp, vp, vp, i64, f32, vp, vp, vp]
+    lib.rt_gate_residual_bwd.restype = ctypes.c_int
+    lib.rt_residual_add.argtypes = [vp, vp, i64, f32, vp, vp]
+    lib.rt_residual_add.restype = ctypes.c_int
+    lib.rt_residual_add_bwd.argtypes = [vp, i64, f32, vp, vp]
+    lib.rt_residual_add_bwd.restype = ctypes.c_int
+    lib.rt_swiglu.argtypes = [vp, i64, i32, vp, vp]
+    lib.rt_swiglu.restype = ctypes.c_int
+    lib.rt_swiglu_bwd.argtypes = [vp, vp, i64, i32, vp, vp]
+    lib.rt_swiglu_bwd.restype = ctypes.c_int
+    lib.rt_column_order_device.argtypes = [vp, vp, i32, i32, vp, vp]
+    lib.rt_column_order_device.restype = ctypes.c_int
     lib.rt_selftest_bounded_wait.argtypes = [ctypes.c_int64, vp, vp]
     lib.rt_selftest_bounded_wait.restype = ctypes.c_int
 

@@ -142,6 +142,20 @@ def build_tile_plan(perm, seq_row_ids, column_ids, is_padding, fk_adj, kind: int
     return TilePlan(kind=kind, batch=b, seq_len=s, max_rows=r, buffer=buf, c=plan)
 
 
+def column_order(column_ids: torch.Tensor, is_padding: torch.Tensor) -> torch.Tensor:
+    """The column kind's cell order (sampler.rs:655-668: padding flag, column
+    id, position) computed on the GPU from [B,S] device tensors; int16 storage
+    of the uint16 order, bit-identical to the host rt_column_order."""
+    lib = _lib.load()
+    cols = column_ids.to(torch.int32).contiguous()
+    pad = is_padding.to(torch.uint8).contiguous()
+    b, s = cols.shape
+    out = torch.empty((b, s), dtype=torch.int16, device=cols.device)
+    _lib.check(lib.rt_column_order_device(cols.data_ptr(), pad.data_ptr(), b, s, out.data_ptr(),
+                                          _stream_ptr(cols.device)), "rt_column_order_device")
+    return out
+
+
 def build_attention_masks(batch: dict, max_rows: int | None = None, kinds=("feature", "neighbor",
                                                                               "column")):
     """Drop-in for model.py:201 ``build_attention_masks(batch, max_rows)``.

@@ -10,3 +10,5 @@
 #include "attn_bwd_noalloc.cu"
 #include "row_order.cu"
 #include "selftest.cu"
+#include "col_sort.cu"
+#include "layer_ops.cu"

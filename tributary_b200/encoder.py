@@ -56,23 +56,42 @@ class EncoderConfig:
 
 class ZeroCenteredRMSNorm(nn.Module):
     """(1 + gamma) * x / sqrt(mean(x^2) + eps), gamma initialised to 0
-    (layers.py:16-30)."""
+    (layers.py:16-30), computed by ``ops.rms_norm`` (the output only feeds
+    matmuls: bf16 under autocast)."""
 
     def __init__(self, d: int, eps: float):
         super().__init__()
         self.gamma = nn.Parameter(torch.zeros(d))
         self.eps = eps
 
-    def forward(self, x):
-        y = F.rms_norm(x.float(), (x.shape[-1],), 1.0 + self.gamma, self.eps)
-        if torch.is_autocast_enabled(x.device.type):  # the output only feeds matmuls
-            y = y.to(torch.get_autocast_dtype(x.device.type))
-        return y
+    def forward(self, x, ops):
+        return ops.rms_norm(x, self.gamma, self.eps)
 
 
 class KernelOps:
-    """The sublayer's token preparation and attention on the library's
-    kernels; ``order`` is the [B,S] int16 cell order, ``ctx`` the TilePlan."""
+    """The encoder's token preparation, attention and fused layer kernels on
+    the library: ``order`` is the [B,S] int16 cell order, ``ctx`` the
+    TilePlan; rms_norm, gate_residual and swiglu are one kernel each way."""
+
+    @staticmethod
+    def rms_norm(x, gamma, eps):
+        from .layer_ops import rms_norm
+        return rms_norm(x, gamma, eps)
+
+    @staticmethod
+    def gate_residual(x, out, gate, scale):
+        from .layer_ops import gate_residual
+        return gate_residual(x, out, gate, scale)
+
+    @staticmethod
+    def swiglu(u):
+        from .layer_ops import swiglu
+        return swiglu(u)
+
+    @staticmethod
+    def residual_add(x, h, scale):
+        from .layer_ops import residual_add
+        return residual_add(x, h, scale)
 
     @staticmethod
     def qk_prepare(qkv, order, tau, heads, head_dim):
@@ -112,18 +131,18 @@ class GatedAttention(nn.Module):
     def forward(self, x, order, mask_ctx, ops):
         cfg = self.cfg
         h, dh = cfg.n_heads, cfg.d_head
-        x_norm = self.norm(x)
+        x_norm = self.norm(x, ops)
         q, k, v = ops.qk_prepare(self.qkv(x_norm), order, self.tau, h, dh)
         o = ops.heads_unpermute(ops.attention(q, k, v, mask_ctx, 1.0 / math.sqrt(dh)), order)
         if not torch.is_autocast_enabled(o.device.type):  # autocast feeds W_O bf16 as it is
             o = o.to(x.dtype)
-        out = self.wo(o) * self.output_scale
-        gate = torch.sigmoid(self.w_gate(x_norm))
-        return x + (out * gate).float()
+        return ops.gate_residual(x, self.wo(o), self.w_gate(x_norm), self.output_scale)
 
 
 class SwiGLU(nn.Module):
-    """W_down (silu(W_gate x) * W_up x), no biases (layers.py:177-200)."""
+    """W_down (silu(W_gate x) * W_up x), no biases (layers.py:177-200); the
+    gate and up projections run as one matmul whose [.., 2 d_ff] output
+    ``ops.swiglu`` turns into the activation."""
 
     def __init__(self, cfg: EncoderConfig, output_scale: float):
         super().__init__()
@@ -133,8 +152,10 @@ class SwiGLU(nn.Module):
         self.w_down = nn.Linear(f, d, bias=False)
         self.output_scale = output_scale
 
-    def forward(self, x):
-        return self.w_down(F.silu(self.w_gate(x)) * self.w_up(x)) * self.output_scale
+    def forward(self, x, ops):
+        """The FFN's output before its residual scale (EncoderLayer adds it)."""
+        u = F.linear(x, torch.cat([self.w_gate.weight, self.w_up.weight], 0))
+        return self.w_down(ops.swiglu(u))
 
 
 class EncoderLayer(nn.Module):
@@ -148,7 +169,7 @@ class EncoderLayer(nn.Module):
     def forward(self, x, masks, ops):
         for sub, (order, ctx) in zip(self.attn, masks):
             x = sub(x, order, ctx, ops)
-        return x + self.ffn(self.ffn_norm(x)).float()
+        return ops.residual_add(x, self.ffn(self.ffn_norm(x, ops), ops), self.ffn.output_scale)
 
 
 class ValueEncoder(nn.Module):
@@ -169,7 +190,7 @@ class ValueEncoder(nn.Module):
         self.mask_emb = nn.Parameter(torch.randn(d) * 0.02)
         self.norm = ZeroCenteredRMSNorm(d, cfg.rms_eps)
 
-    def forward(self, cells, col_table, cat_table):
+    def forward(self, cells, col_table, cat_table, ops):
         col = self.column_name(col_table[cells["column_ids"]])
         vals = torch.stack([
             self.identifier.expand_as(col).to(col.dtype),
@@ -187,14 +208,14 @@ class ValueEncoder(nn.Module):
         is_target = cells["is_target"][..., None].to(raw.dtype)
         v = is_null * self.null_emb.to(raw.dtype) + (1 - is_null) * raw
         v = is_target * self.mask_emb.to(raw.dtype) + (1 - is_target) * v
-        return self.norm(col + v).float()  # the residual stream stays fp32
+        return self.norm(col + v, ops).float()  # the residual stream stays fp32
 
 
 class RTEncoder(nn.Module):
     """Value encoder -> layers -> final norm -> decoder heads (model.py:267-321).
 
-    ``ops`` (qk_prepare, attention, heads_unpermute) defaults to the library
-    kernels (KernelOps); each entry of ``masks`` passed to forward is
+    ``ops`` (qk_prepare, attention, heads_unpermute, rms_norm, gate_residual,
+    swiglu, residual_add) defaults to the library kernels (KernelOps); each entry of ``masks`` passed to forward is
     (cell order, mask context) for one sublayer kind -- for KernelOps the
     int16 order and the kind's TilePlan (train.build_masks).
     """
@@ -214,10 +235,10 @@ class RTEncoder(nn.Module):
         self.categorical_head = nn.Linear(d, d)
 
     def forward(self, cells, masks, col_table, cat_table):
-        x = self.value_encoder(cells, col_table, cat_table)
+        x = self.value_encoder(cells, col_table, cat_table, self.ops)
         for layer in self.layers:
             x = layer(x, masks, self.ops)
-        x = self.final_norm(x)
+        x = self.final_norm(x, self.ops)
         return {
             "null": self.null_head(x).squeeze(-1),
             "num": self.numerical_head(x).squeeze(-1),

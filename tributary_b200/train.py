@@ -288,14 +288,18 @@ def build_masks(meta: dict, kinds, max_rows: int | None = None):
     """Per sublayer kind: (int16 cell order, tile plan), on the device of
     ``meta`` (batch.make_cells arrays moved to the GPU). The plans are rebuilt
     for every batch, as build_attention_masks is inside the reference's jitted
-    step (model.py:299-313)."""
+    step (model.py:299-313). The column kind's order is sorted on the GPU; the
+    feature / neighbor orders (reverse Cuthill-McKee, sequential per sample)
+    come with the batch."""
     from . import attention as rt
     from .batch import MASK_COLUMN, MASK_FEATURE, MASK_NEIGHBOR
     from .tokens import _order16
-    key = {MASK_COLUMN: "col_perm", MASK_FEATURE: "out_perm", MASK_NEIGHBOR: "in_perm"}
+    key = {MASK_FEATURE: "out_perm", MASK_NEIGHBOR: "in_perm"}
     out = []
     for kind in kinds:
-        if kind in key:
+        if kind == MASK_COLUMN:  # sorted on the GPU from the batch's own tensors
+            order = rt.column_order(meta["column_ids"], meta["is_padding"])
+        elif kind in key:
             order = _order16(meta[key[kind]])
         else:
             b, s = meta["seq_row_ids"].shape
