@@ -51,10 +51,11 @@ FLOPS_PER_LIVE_TILE = {"fwd": 4, "bwd": 10}  # x 128^2 x Dh per live (b, h, tile
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one dkdvq_kernel
 # launch -- the fused dK/dV/dQ backward, the dominant kernel -- from an ncu
-# capture of this workload (summarised under profiles/); about the same for
-# every mask kind: q, k, v, dO and the row statistics read once, dK and dV
-# written once, plus the fp32 dQ accumulator's L2 misses under the reduce-adds.
-NCU_DKDVQ_TRAFFIC = {"rt_attn_fwd_bwd_b8_s4096_h16_d64": 647.0e6}
+# capture of the full-mask launch at B = 4 (301.9 MB, summarised under
+# profiles/) scaled by 2 to this workload's B = 8 launch: q, k, v, dO and the
+# row statistics read once, dK and dV written once, plus the fp32 dQ
+# accumulator's L2 misses under the reduce-adds.
+NCU_DKDVQ_TRAFFIC = {"rt_attn_fwd_bwd_b8_s4096_h16_d64": 603.8e6}
 
 
 def measured_peaks():
