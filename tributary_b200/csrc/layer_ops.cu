@@ -161,14 +161,26 @@ __global__ void __launch_bounds__(256) rms_norm_bwd_kernel(const uint16_t* __res
   }
 }
 
-// dgamma[c] = sum over the blocks' partials, in block order.
+// dgamma[c] = sum over the blocks' partials: a block takes 32 columns, its
+// eight warps each sum every eighth partial (lane = column), and the eight
+// warp sums are added in warp order -- a fixed order, so the result is
+// deterministic.
 __global__ void __launch_bounds__(256) sum_partials_kernel(const float* __restrict__ part, int nparts, int d,
                                                            float* __restrict__ out) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= d) return;
+  __shared__ float sw[8][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lane;
   float s = 0.f;
-  for (int p = 0; p < nparts; ++p) s += part[(size_t)p * d + c];
-  out[c] = s;
+  if (c < d)
+    for (int p = warp; p < nparts; p += 8) s += part[(size_t)p * d + c];
+  sw[warp][lane] = s;
+  __syncthreads();
+  if (warp == 0 && c < d) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += sw[w][lane];
+    out[c] = t;
+  }
 }
 
 __global__ void __launch_bounds__(256) gate_residual_kernel(const float* __restrict__ x, const uint16_t* __restrict__ o,
@@ -313,7 +325,7 @@ extern "C" int rt_rms_norm_bwd(const uint16_t* dy, const float* x, const float* 
   if (gpl <= 2) layer::rms_norm_bwd_kernel<2><<<blocks, 256, 0, s>>>(dy, x, gamma, rstd, rows, d, dx, part);
   else layer::rms_norm_bwd_kernel<4><<<blocks, 256, 0, s>>>(dy, x, gamma, rstd, rows, d, dx, part);
   if (int st = check_launch("rms_norm_bwd_kernel launch")) return st;
-  layer::sum_partials_kernel<<<(d + 255) / 256, 256, 0, s>>>(part, blocks, d, dgamma);
+  layer::sum_partials_kernel<<<(d + 31) / 32, 256, 0, s>>>(part, blocks, d, dgamma);
   return check_launch("sum_partials_kernel launch");
 }
 
