@@ -218,6 +218,8 @@ __global__ void __launch_bounds__(128) tile_mask_kernel(
 }
 
 // Single block: CSR lists (q2k over (b,qt) rows, k2q over (b,kt) rows) from the bitmaps.
+constexpr int kListSmemBytes = 96 * 1024;  // tile_list_kernel's staged bitmaps
+
 __global__ void __launch_bounds__(1024) tile_list_kernel(rt_tile_plan plan) {
   const int T = plan.tiles;
   const int W = plan.words;
@@ -228,6 +230,22 @@ __global__ void __launch_bounds__(1024) tile_list_kernel(rt_tile_plan plan) {
   const int r1 = min(nrows, r0 + chunk);
   __shared__ int s_warp[32];
   __shared__ int s_total;
+  // the bitmaps (a few KB) in shared memory when they fit: every row and
+  // column scan below reads them many times
+  extern __shared__ uint32_t s_bits[];
+  const int nwords = nrows * W;
+  const bool staged = 2LL * nwords * (long long)sizeof(uint32_t) <= (long long)kListSmemBytes;
+  const uint32_t* live = plan.live_bits;
+  const uint32_t* full_b = plan.full_bits;
+  if (staged) {
+    for (int i = threadIdx.x; i < nwords; i += blockDim.x) {
+      s_bits[i] = plan.live_bits[i];
+      s_bits[nwords + i] = plan.full_bits[i];
+    }
+    __syncthreads();
+    live = s_bits;
+    full_b = s_bits + nwords;
+  }
 
   for (int pass = 0; pass < 2; ++pass) {
     const bool by_q = pass == 0;
@@ -237,10 +255,10 @@ __global__ void __launch_bounds__(1024) tile_list_kernel(rt_tile_plan plan) {
     for (int r = r0; r < r1; ++r) {
       const int b = r / T, x = r % T;
       if (by_q) {
-        for (int w = 0; w < W; ++w) local += __popc(plan.live_bits[((size_t)b * T + x) * W + w]);
+        for (int w = 0; w < W; ++w) local += __popc(live[((size_t)b * T + x) * W + w]);
       } else {
         for (int q = 0; q < T; ++q)
-          local += (plan.live_bits[((size_t)b * T + q) * W + (x >> 5)] >> (x & 31)) & 1u;
+          local += (live[((size_t)b * T + q) * W + (x >> 5)] >> (x & 31)) & 1u;
       }
     }
     // exclusive block scan of `local`
@@ -273,16 +291,16 @@ __global__ void __launch_bounds__(1024) tile_list_kernel(rt_tile_plan plan) {
       if (by_q) {
         for (int kt = 0; kt < T; ++kt) {
           const size_t wi = ((size_t)b * T + x) * W + (kt >> 5);
-          if ((plan.live_bits[wi] >> (kt & 31)) & 1u) {
-            const bool full = (plan.full_bits[wi] >> (kt & 31)) & 1u;
+          if ((live[wi] >> (kt & 31)) & 1u) {
+            const bool full = (full_b[wi] >> (kt & 31)) & 1u;
             idx[pos++] = kt | (full ? (int)0x80000000u : 0);
           }
         }
       } else {
         for (int qt = 0; qt < T; ++qt) {
           const size_t wi = ((size_t)b * T + qt) * W + (x >> 5);
-          if ((plan.live_bits[wi] >> (x & 31)) & 1u) {
-            const bool full = (plan.full_bits[wi] >> (x & 31)) & 1u;
+          if ((live[wi] >> (x & 31)) & 1u) {
+            const bool full = (full_b[wi] >> (x & 31)) & 1u;
             idx[pos++] = qt | (full ? (int)0x80000000u : 0);
           }
         }
@@ -333,7 +351,20 @@ int launch_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids, co
   else
     tile_mask_kernel<RT_MASK_FULL, false><<<grid, RT_TILE, 0, stream>>>(perm, seq_row_ids, column_ids,
                                                                         is_padding, fk_bits, S, R, WR, plan);
-  tile_list_kernel<<<1, 1024, 0, stream>>>(plan);
+  {
+    const size_t bits_bytes = 2 * sizeof(uint32_t) * (size_t)B * plan.tiles * plan.words;
+    const size_t smem = bits_bytes <= (size_t)kListSmemBytes ? bits_bytes : 0;
+    static bool list_configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !list_configured[dev]) {
+      const cudaError_t e =
+          cudaFuncSetAttribute(tile_list_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kListSmemBytes);
+      if (e != cudaSuccess) return cuda_failure(e, "cudaFuncSetAttribute(tile_list_kernel)");
+      list_configured[dev] = true;
+    }
+    tile_list_kernel<<<1, 1024, smem, stream>>>(plan);
+  }
   return check_launch("tile plan kernels launch");
 }
 
