@@ -173,12 +173,10 @@ class Workload:
             grads = [torch.empty_like(dev["q"]) for _ in range(3)]
             ws = torch.empty(rt._lib.load().rt_attention_bwd_workspace_bytes(B, H, S),
                              dtype=torch.uint8, device=device)
-            ws_fwd = torch.empty(rt._lib.load().rt_attention_fwd_workspace_bytes(), dtype=torch.uint8,
-                                 device=device)
             pinned = {n: t.pin_memory() for n, t in host.items()}
             out_pinned = [torch.empty_like(host["q"]).pin_memory() for _ in range(4)]
             self.kinds.append(dict(kind=kind, dev=dev, plan=plan, o=o, lse=lse, grads=grads, ws=ws,
-                                   ws_fwd=ws_fwd, pinned=pinned, out_pinned=out_pinned))
+                                   pinned=pinned, out_pinned=out_pinned))
         torch.cuda.synchronize()
         self.nnz = [k["plan"].nnz() for k in self.kinds]
         self.tiles = self.kinds[0]["plan"].tiles
@@ -210,7 +208,7 @@ class Workload:
             if events is not None:
                 events["plan"][1].record()
                 events["fwd"][0].record()
-            rt.attention_fwd(d["q"], d["k"], d["v"], k["plan"], scale, out=k["o"], lse=k["lse"], workspace=k["ws_fwd"])
+            rt.attention_fwd(d["q"], d["k"], d["v"], k["plan"], scale, out=k["o"], lse=k["lse"])
             if events is not None:
                 events["fwd"][1].record()
                 events["bwd"][0].record()
@@ -237,7 +235,7 @@ class Workload:
                 d[n].copy_(p[n], non_blocking=True)
                 h2d += p[n].numel() * p[n].element_size()
             self.rebuild_plan(k)
-            rt.attention_fwd(d["q"], d["k"], d["v"], k["plan"], scale, out=k["o"], lse=k["lse"], workspace=k["ws_fwd"])
+            rt.attention_fwd(d["q"], d["k"], d["v"], k["plan"], scale, out=k["o"], lse=k["lse"])
             rt.attention_bwd(d["q"], d["k"], d["v"], k["o"], k["lse"], d["do"], k["plan"], scale,
                              dq=k["grads"][0], dk=k["grads"][1], dv=k["grads"][2], workspace=k["ws"])
             for dst, src in zip(k["out_pinned"], [k["o"]] + k["grads"]):
@@ -272,7 +270,7 @@ class Workload:
                 if ev["out"] is not None:
                     s_comp.wait_event(ev["out"])  # previous step's outputs have been read back
                 self.rebuild_plan(k)
-                rt.attention_fwd(d["q"], d["k"], d["v"], k["plan"], scale, out=k["o"], lse=k["lse"], workspace=k["ws_fwd"])
+                rt.attention_fwd(d["q"], d["k"], d["v"], k["plan"], scale, out=k["o"], lse=k["lse"])
                 rt.attention_bwd(d["q"], d["k"], d["v"], k["o"], k["lse"], d["do"], k["plan"], scale,
                                  dq=k["grads"][0], dk=k["grads"][1], dv=k["grads"][2], workspace=k["ws"])
                 ev["comp"] = torch.cuda.Event()

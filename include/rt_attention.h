@@ -178,20 +178,6 @@ int rt_attention_fwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, in
  * then the fp32 dQ accumulator [batch*heads][seq_len rounded up][64] of the
  * fused dK/dV/dQ pass, then that pass's row-statistic operand rows
  * [batch*heads][seq_len rounded up][16] bf16. */
-/* rt_attention_fwd with a work counter in `workspace` (device memory,
- * 16-byte aligned, rt_attention_fwd_workspace_bytes() bytes, reset on the
- * stream by each call): the persistent kernel's CTAs take work items
- * (b, h, q-tile) from it in order as they finish their previous ones, instead
- * of a fixed round-robin share, which evens out items of different live-tile
- * counts. Same results, bit for bit. Calls that overlap on the GPU need
- * separate workspaces. No counterpart in the reference (its attention is one
- * dense XLA computation). */
-size_t rt_attention_fwd_workspace_bytes(void);
-int rt_attention_fwd_ws(const uint16_t* q, const uint16_t* k, const uint16_t* v, int32_t batch,
-                        int32_t heads, int32_t seq_len, int32_t head_dim, float scale,
-                        const rt_tile_plan* plan, uint16_t* o, float* lse, void* workspace,
-                        size_t workspace_bytes, void* stream);
-
 size_t rt_attention_bwd_workspace_bytes(int32_t batch, int32_t heads, int32_t seq_len);
 
 /* Backward: the gradients jax autodiff takes through layers.py:83-94.

@@ -115,16 +115,15 @@ int main(int argc, char** argv) {
   CHECK_RT(rt_build_tile_plan((const uint16_t*)perm, (const uint16_t*)rows, (const int32_t*)cols,
                               (const uint8_t*)pad, (const uint8_t*)fk, B, S, R, kind, &plan, stream));
 
-  void *o = NULL, *lse = NULL, *dq = NULL, *dk = NULL, *dv = NULL, *ws = NULL, *ws_fwd = NULL;
+  void *o = NULL, *lse = NULL, *dq = NULL, *dk = NULL, *dv = NULL, *ws = NULL;
   const size_t ws_bytes = rt_attention_bwd_workspace_bytes(B, H, S);
   CHECK(cudaMalloc(&o, 2 * elems) == cudaSuccess && cudaMalloc(&lse, 4 * (size_t)B * H * S) == cudaSuccess &&
             cudaMalloc(&dq, 2 * elems) == cudaSuccess && cudaMalloc(&dk, 2 * elems) == cudaSuccess &&
-            cudaMalloc(&dv, 2 * elems) == cudaSuccess && cudaMalloc(&ws, ws_bytes) == cudaSuccess &&
-            cudaMalloc(&ws_fwd, rt_attention_fwd_workspace_bytes()) == cudaSuccess,
+            cudaMalloc(&dv, 2 * elems) == cudaSuccess && cudaMalloc(&ws, ws_bytes) == cudaSuccess,
         104);
   const float scale = 1.0f / sqrtf((float)Dh);
-  CHECK_RT(rt_attention_fwd_ws((const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, B, H, S, Dh, scale, &plan,
-                               (uint16_t*)o, (float*)lse, ws_fwd, rt_attention_fwd_workspace_bytes(), stream));
+  CHECK_RT(rt_attention_fwd((const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, B, H, S, Dh, scale, &plan,
+                            (uint16_t*)o, (float*)lse, stream));
   CHECK_RT(rt_attention_bwd((const uint16_t*)q, (const uint16_t*)k, (const uint16_t*)v, (const uint16_t*)o,
                             (const uint16_t*)d_o, (const float*)lse, B, H, S, Dh, scale, &plan, (uint16_t*)dq,
                             (uint16_t*)dk, (uint16_t*)dv, ws, ws_bytes, stream));

@@ -100,22 +100,3 @@ def test_wide_logit_rows_take_the_exact_path(cuda_lib):
     for got, ref in zip((dq, dk, dv), c.oracle_bwd()):
         g = from_bf16_tensor(got)
         assert np.isfinite(g).all()
-
-
-def test_work_counter_schedule_matches_round_robin(cuda_lib):
-    """The forward's CTAs take work items from a counter (rt_attention_fwd_ws)
-    instead of a fixed round-robin share (rt_attention_fwd): which CTA runs an
-    item changes, the item's arithmetic does not, so o and lse are identical
-    bit for bit. 512 items, several per CTA."""
-    import torch
-    from tributary_b200 import _lib
-    from tributary_b200.attention import attention_fwd, device_status
-    c = Case((48, 2, 2048, 6, 4, 16, 0.9, 0.05, None, None, 2), 1, h=16, dh=64, seed=48)
-    o1, l1 = attention_fwd(c.qd, c.kd, c.vd, c.plan, c.scale)
-    o2, l2 = torch.empty_like(o1), torch.empty_like(l1)
-    _lib.check(_lib.load().rt_attention_fwd(
-        c.qd.data_ptr(), c.kd.data_ptr(), c.vd.data_ptr(), c.b, c.h, c.s, c.dh, float(c.scale),
-        __import__("ctypes").byref(c.plan.c), o2.data_ptr(), l2.data_ptr(),
-        torch.cuda.current_stream().cuda_stream), "rt_attention_fwd")
-    assert device_status() == 0
-    assert torch.equal(o1, o2) and torch.equal(l1, l2)

@@ -73,12 +73,6 @@ def test_argument_validation_before_device_work(lib):
     # unsupported head_dim is reported as such
     assert lib.rt_attention_fwd(fake, fake, fake, 1, 1, 128, 48, 1.0, ctypes.byref(plan),
                                 fake, fake, None) == _lib.RT_ERR_UNSUPPORTED
-    # the work-counter forward wants its workspace
-    ws_bytes = lib.rt_attention_fwd_workspace_bytes()
-    assert lib.rt_attention_fwd_ws(fake, fake, fake, 1, 1, 128, 64, 0.125, ctypes.byref(plan), fake, fake,
-                                   None, ws_bytes, None) == _lib.RT_ERR_INVALID_ARGUMENT
-    assert lib.rt_attention_fwd_ws(fake, fake, fake, 1, 1, 128, 64, 0.125, ctypes.byref(plan), fake, fake,
-                                   fake, ws_bytes - 1, None) == _lib.RT_ERR_WORKSPACE
     # a scale that is not positive and finite
     for bad in (0.0, -0.125, float("nan"), float("inf")):
         assert lib.rt_attention_fwd(fake, fake, fake, 1, 1, 128, 64, bad, ctypes.byref(plan),

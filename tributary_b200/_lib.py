@@ -36,7 +36,6 @@ EXPORTED = (
     "rt_selftest_bounded_wait", "rt_column_order_device",
     "rt_rms_norm", "rt_rms_norm_bwd_workspace_bytes", "rt_rms_norm_bwd", "rt_gate_residual",
     "rt_gate_residual_bwd", "rt_swiglu", "rt_swiglu_bwd", "rt_residual_add", "rt_residual_add_bwd",
-    "rt_attention_fwd_workspace_bytes", "rt_attention_fwd_ws",
 )
 
 
@@ -92,10 +91,6 @@ def _declare(lib):
     lib.rt_rcm_order.restype = ctypes.c_int
     lib.rt_attention_fwd.argtypes = [vp, vp, vp, i32, i32, i32, i32, f32, plan_p, vp, vp, vp]
     lib.rt_attention_fwd.restype = ctypes.c_int
-    lib.rt_attention_fwd_workspace_bytes.argtypes = []
-    lib.rt_attention_fwd_workspace_bytes.restype = sz
-    lib.rt_attention_fwd_ws.argtypes = [vp, vp, vp, i32, i32, i32, i32, f32, plan_p, vp, vp, vp, sz, vp]
-    lib.rt_attention_fwd_ws.restype = ctypes.c_int
     lib.rt_attention_bwd_workspace_bytes.argtypes = [i32, i32, i32]
     lib.rt_attention_bwd_workspace_bytes.restype = sz
     lib.rt_attention_bwd.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, plan_p,

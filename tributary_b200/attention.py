@@ -200,11 +200,9 @@ def _check_qkv(q, k, v, plan: TilePlan):
     return b, h, s, dh
 
 
-def attention_fwd(q, k, v, plan: TilePlan, scale: float | None = None, out=None, lse=None, workspace=None):
+def attention_fwd(q, k, v, plan: TilePlan, scale: float | None = None, out=None, lse=None):
     """o, lse = masked softmax attention of already-normalised q_hat (tau folded
-    in), k_hat, v: [B,H,S,Dh] bf16 in the plan's permuted token order. The
-    kernel's CTAs take work items from a counter in ``workspace`` (allocated
-    here when not given; calls overlapping on the GPU need separate ones)."""
+    in), k_hat, v: [B,H,S,Dh] bf16 in the plan's permuted token order."""
     b, h, s, dh = _check_qkv(q, k, v, plan)
     if scale is None:
         scale = 1.0 / math.sqrt(dh)
@@ -212,13 +210,9 @@ def attention_fwd(q, k, v, plan: TilePlan, scale: float | None = None, out=None,
         out = torch.empty_like(q)
     if lse is None:
         lse = torch.empty((b, h, s), dtype=torch.float32, device=q.device)
-    lib = _lib.load()
-    if workspace is None:
-        workspace = torch.empty(lib.rt_attention_fwd_workspace_bytes(), dtype=torch.uint8, device=q.device)
-    _lib.check(lib.rt_attention_fwd_ws(
+    _lib.check(_lib.load().rt_attention_fwd(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), b, h, s, dh, float(scale), ctypes.byref(plan.c),
-        out.data_ptr(), lse.data_ptr(), workspace.data_ptr(), workspace.numel(), _stream_ptr(q.device)),
-        "rt_attention_fwd_ws")
+        out.data_ptr(), lse.data_ptr(), _stream_ptr(q.device)), "rt_attention_fwd")
     return out, lse
 
 

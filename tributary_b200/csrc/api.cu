@@ -252,10 +252,9 @@ int rt_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids, const 
                                 max_rows, kind, *plan, static_cast<cudaStream_t>(stream));
 }
 
-namespace {
-int attention_fwd_common(const uint16_t* q, const uint16_t* k, const uint16_t* v, int32_t batch, int32_t heads,
-                         int32_t seq_len, int32_t head_dim, float scale, const rt_tile_plan* plan, uint16_t* o,
-                         float* lse, int* work_counter, void* stream) {
+int rt_attention_fwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, int32_t batch,
+                     int32_t heads, int32_t seq_len, int32_t head_dim, float scale,
+                     const rt_tile_plan* plan, uint16_t* o, float* lse, void* stream) {
   if (batch < 0 || heads < 0 || seq_len < 0 || seq_len > 65536 || batch > 65535 || heads > 65535)
     return RT_ERR_INVALID_ARGUMENT;
   if (head_dim != 32 && head_dim != 64) return RT_ERR_UNSUPPORTED;
@@ -268,27 +267,8 @@ int attention_fwd_common(const uint16_t* q, const uint16_t* k, const uint16_t* v
     return RT_ERR_INVALID_ARGUMENT;
   DeviceGuard guard(q);
   if (guard.status() != RT_OK) return guard.status();
-  return launch_attention_fwd(q, k, v, batch, heads, seq_len, head_dim, scale, *plan, o, lse, work_counter,
+  return launch_attention_fwd(q, k, v, batch, heads, seq_len, head_dim, scale, *plan, o, lse,
                               static_cast<cudaStream_t>(stream));
-}
-}  // namespace
-
-int rt_attention_fwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, int32_t batch,
-                     int32_t heads, int32_t seq_len, int32_t head_dim, float scale,
-                     const rt_tile_plan* plan, uint16_t* o, float* lse, void* stream) {
-  return attention_fwd_common(q, k, v, batch, heads, seq_len, head_dim, scale, plan, o, lse, nullptr, stream);
-}
-
-size_t rt_attention_fwd_workspace_bytes(void) { return 256; }
-
-int rt_attention_fwd_ws(const uint16_t* q, const uint16_t* k, const uint16_t* v, int32_t batch,
-                        int32_t heads, int32_t seq_len, int32_t head_dim, float scale,
-                        const rt_tile_plan* plan, uint16_t* o, float* lse, void* workspace,
-                        size_t workspace_bytes, void* stream) {
-  if (!workspace || !aligned16(workspace)) return RT_ERR_INVALID_ARGUMENT;
-  if (workspace_bytes < rt_attention_fwd_workspace_bytes()) return RT_ERR_WORKSPACE;
-  return attention_fwd_common(q, k, v, batch, heads, seq_len, head_dim, scale, plan, o, lse,
-                              static_cast<int*>(workspace), stream);
 }
 
 namespace {

@@ -156,12 +156,6 @@ constexpr int kMainTmemCols = 512;
 constexpr int kOMain = kSets * 128;
 constexpr int kStages = 4;
 constexpr int kInfoRing = 8;
-// Work items reach the CTA through a ring of item ids in shared memory: the
-// producer takes them (the next index of a work counter when the caller gives
-// one, else blockIdx.x + j * gridDim.x), one entry per item, -1 after the last;
-// every other role reads item k's id from the ring and releases it when done.
-constexpr int kItemRing = 8;
-constexpr int kItemReaders = 2 + 4 + 12;  // warps that release each item: PV, S, epilogue, softmax
 constexpr int kMaskBytes = RT_TILE * 16;
 // tile-info word: kt (bits 0-15), fully live (16), first tile of its item (17),
 // last tile of its item (18)
@@ -190,7 +184,6 @@ struct __align__(8) MainBarriers {
   uint64_t item_done[2], o_free[2];
   uint64_t sdiag_full[2], lsum_full[2];
   uint64_t drain, drain_s;
-  uint64_t item_full[kItemRing], item_empty[kItemRing];
 };
 
 struct ItemCoord {
@@ -229,7 +222,7 @@ __global__ void __launch_bounds__(kMainThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const uint16_t* __restrict__ qg,
                     const uint16_t* __restrict__ kg, const rt_tile_plan plan, int H, int S, float scale_log2,
-                    uint16_t* __restrict__ out, float* __restrict__ lse, int* __restrict__ work_counter) {
+                    uint16_t* __restrict__ out, float* __restrict__ lse) {
   using C = MainCfg<DH>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -239,20 +232,14 @@ __global__ void __launch_bounds__(kMainThreads, 1)
   __shared__ uint32_t s_info[kInfoRing];
   __shared__ float s_sdiag[2][RT_TILE];
   __shared__ float s_lpart[2][kSets][RT_TILE];
-  __shared__ int s_item[kItemRing];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int T = plan.tiles;
   const int n_items_total = plan.batch * H * T;
   const int G = gridDim.x;
-  // id of this CTA's k-th item (-1: none left), once the producer has published it
-  auto item_at = [&](int k, bool& ok) -> int {
-    if (!ok) return -1;
-    if (!(ok = mbar_wait_warp(&bars.item_full[k % kItemRing], (k / kItemRing) & 1, &abort_flag))) return -1;
-    return *reinterpret_cast<volatile int*>(&s_item[k % kItemRing]);
-  };
-  auto item_release = [&](int k) { mbar_arrive_warp(&bars.item_empty[k % kItemRing]); };
+  const int n_items = (n_items_total - (int)blockIdx.x + G - 1) / G;  // items of this CTA
+  auto item_id = [&](int k) { return (int)blockIdx.x + k * G; };
   auto item_ntiles = [&](int item) {
     const ItemCoord ic = item_coord(item, H, T);
     const int r = ic.b * T + ic.qt;
@@ -280,10 +267,6 @@ __global__ void __launch_bounds__(kMainThreads, 1)
     }
     mbar_init(&bars.drain, 1);
     mbar_init(&bars.drain_s, 1);
-    for (int i = 0; i < kItemRing; ++i) {
-      mbar_init(&bars.item_full[i], 1);
-      mbar_init(&bars.item_empty[i], kItemReaders);
-    }
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -299,58 +282,27 @@ __global__ void __launch_bounds__(kMainThreads, 1)
     // ---------------- producer ----------------
     // item k's row pointer and first 32 list entries are loaded while item
     // k-1 streams, so item boundaries cost no L2 round trip
-    auto item_list = [&](int id, int& lb, int& n, int& ent0) {
+    auto item_list = [&](int k, int& lb, int& n, int& ent0) {
       lb = 0;
       n = 0;
       ent0 = 0;
-      if (id < 0) return;
-      const ItemCoord ic = item_coord(id, H, T);
+      if (k >= n_items) return;
+      const ItemCoord ic = item_coord(item_id(k), H, T);
       const int r = ic.b * T + ic.qt;
       lb = __ldg(plan.q2k_ptr + r);
       n = __ldg(plan.q2k_ptr + r + 1) - lb;
       ent0 = lane < n ? __ldg(plan.q2k_idx + lb + lane) : 0;
     };
-    bool ok = true;
-    // publish item ids up to index `upto` (exclusive), stopping after the -1
-    int published = 0;
-    bool ended = false;
-    auto publish = [&](int upto) {
-      while (ok && !ended && published < upto) {
-        const int j = published;
-        if (j >= kItemRing &&
-            !(ok = mbar_wait_warp(&bars.item_empty[j % kItemRing], ((j / kItemRing) - 1) & 1, &abort_flag)))
-          break;
-        int id = 0;
-        if (lane == 0) {
-          id = work_counter != nullptr ? atomicAdd(work_counter, 1) : (int)blockIdx.x + j * G;
-          if (id >= n_items_total) id = -1;
-          s_item[j % kItemRing] = id;
-          mbar_arrive(&bars.item_full[j % kItemRing]);
-        }
-        id = __shfl_sync(0xFFFFFFFFu, id, 0);
-        ++published;
-        ended = id < 0;
-      }
-    };
-    auto own_item = [&](int k) {  // an id this warp published (k < published)
-      __syncwarp();
-      return *reinterpret_cast<volatile int*>(&s_item[k % kItemRing]);
-    };
     int g = 0;   // global tile index
     int kq = 0;  // Q loads issued
-    publish(3);
-    int id_k = ok ? own_item(0) : -1;
+    bool ok = true;
     int lb_next, n_next, ent_next;
-    item_list(id_k, lb_next, n_next, ent_next);
-    for (int k = 0; ok && id_k >= 0; ++k) {
-      // ids two items ahead: the epilogue computes the diagonal logits of item k + 2
-      publish(k + 3);
-      if (!ok) break;
-      const int id_next = own_item(k + 1);
+    item_list(0, lb_next, n_next, ent_next);
+    for (int k = 0; ok && k < n_items; ++k) {
       const int lb = lb_next, n = n_next;
       int ent_l = ent_next;
-      item_list(id_next, lb_next, n_next, ent_next);
-      const ItemCoord ic = item_coord(id_k, H, T);
+      item_list(k + 1, lb_next, n_next, ent_next);
+      const ItemCoord ic = item_coord(item_id(k), H, T);
       const int bh = ic.b * H + ic.h;
       const int r = ic.b * T + ic.qt;
       if (k >= 2 && !(ok = mbar_wait_warp(&bars.q_empty[k & 1], ((k - 2) >> 1) & 1, &abort_flag))) break;
@@ -383,7 +335,6 @@ __global__ void __launch_bounds__(kMainThreads, 1)
           __syncwarp();
         }
       }
-      id_k = id_next;
     }
     // drain: every load issued must land before the CTA exits
     volatile int no_abort = 0;
@@ -401,13 +352,10 @@ __global__ void __launch_bounds__(kMainThreads, 1)
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, DH, false, true);
       bool ok = true;
       int kP = 0, g = 0;
-      int idP = item_at(0, ok);
-      int nP_next = idP >= 0 ? item_ntiles(idP) : 0;
-      for (; ok && idP >= 0; ++kP) {
+      int nP_next = n_items > 0 ? item_ntiles(item_id(0)) : 0;
+      for (; ok && kP < n_items; ++kP) {
         const int n = nP_next;
-        const int idP_next = item_at(kP + 1, ok);
-        if (!ok) break;
-        nP_next = idP_next >= 0 ? item_ntiles(idP_next) : 0;
+        nP_next = kP + 1 < n_items ? item_ntiles(item_id(kP + 1)) : 0;
         const int ob = kP & 1;
         if (kP >= 2 && !(ok = mbar_wait_warp(&bars.o_free[ob], ((kP - 2) >> 1) & 1, &abort_flag))) break;
         for (int t = 0; ok && t < n; ++t, ++g) {
@@ -431,8 +379,6 @@ __global__ void __launch_bounds__(kMainThreads, 1)
           if (leader) mma_commit(&bars.item_done[ob]);
           __syncwarp();
         }
-        item_release(kP);
-        idP = idP_next;
       }
       if (leader) mma_commit(&bars.drain);
       __syncwarp();
@@ -445,24 +391,19 @@ __global__ void __launch_bounds__(kMainThreads, 1)
     constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false, false);
     bool ok = true;
     int kS = 0, tS = 0, gS = 0;
-    int idS = item_at(0, ok);
-    int nS = idS >= 0 ? item_ntiles(idS) : 0;
-    int idS_next = idS >= 0 ? item_at(1, ok) : -1;
-    int nS_next = idS_next >= 0 ? item_ntiles(idS_next) : 0;
+    int nS = n_items > 0 ? item_ntiles(item_id(0)) : 0;
+    int nS_next = n_items > 1 ? item_ntiles(item_id(1)) : 0;
     while (ok) {
-      while (idS >= 0 && tS >= nS) {  // leave finished (or empty) items, releasing their Q slot
+      while (kS < n_items && tS >= nS) {  // leave finished (or empty) items, releasing their Q slot
         if (nS == 0 && !(ok = mbar_wait_warp(&bars.q_full[kS & 1], (kS >> 1) & 1, &abort_flag))) break;
         if (leader) mma_commit(&bars.q_empty[kS & 1]);
         __syncwarp();
-        item_release(kS);
         ++kS;
         tS = 0;
-        idS = idS_next;
         nS = nS_next;
-        idS_next = idS >= 0 ? item_at(kS + 1, ok) : -1;
-        nS_next = idS_next >= 0 ? item_ntiles(idS_next) : 0;
+        nS_next = kS + 1 < n_items ? item_ntiles(item_id(kS + 1)) : 0;
       }
-      if (!ok || idS < 0) break;
+      if (!ok || kS >= n_items) break;
       if (tS == 0 && !(ok = mbar_wait_warp(&bars.q_full[kS & 1], (kS >> 1) & 1, &abort_flag))) break;
       const int st = gS % kStages;
       if (!(ok = mbar_wait_warp(&bars.kv_full[st], (gS / kStages) & 1, &abort_flag))) break;
@@ -492,38 +433,27 @@ __global__ void __launch_bounds__(kMainThreads, 1)
     const int row = quad * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const float c = scale_log2;
-    auto put_sdiag = [&](int k, int id) {
-      const ItemCoord ic = item_coord(id, H, T);
+    auto put_sdiag = [&](int k) {
+      const ItemCoord ic = item_coord(item_id(k), H, T);
       const int qrow = ic.qt * RT_TILE + row;
       s_sdiag[k & 1][row] =
           qrow < S ? diag_logit<DH>(qg, kg, ((size_t)(ic.b * H + ic.h)) * S + qrow) : 0.f;
       mbar_arrive_warp(&bars.sdiag_full[k & 1]);
     };
+    for (int k = 0; k < 2 && k < n_items; ++k) put_sdiag(k);
     bool ok = true;
-    int idk = item_at(0, ok);
-    int idk1 = idk >= 0 ? item_at(1, ok) : -1;
-    if (idk >= 0) put_sdiag(0, idk);
-    if (idk1 >= 0) put_sdiag(1, idk1);
-    int g_item = 0;  // global tile index of the current item's first tile
-    for (int k = 0; ok && idk >= 0; ++k) {
-      const int item = idk;
+    for (int k = 0; ok && k < n_items; ++k) {
+      const int item = item_id(k);
       const ItemCoord ic = item_coord(item, H, T);
       const int bh = ic.b * H + ic.h;
       const int qrow = ic.qt * RT_TILE + row;
       const int n = item_ntiles(item);
       if (!(ok = mbar_wait_warp(&bars.lsum_full[k & 1], (k >> 1) & 1, &abort_flag))) break;
-      // the sets' partial sums in the order of the item's tiles (the set that
-      // took tile 0 first), so that l -- and o, lse -- do not depend on where
-      // the item fell in this CTA's sequence of tiles (which CTA ran it)
-      const int r0 = g_item % kSets;
-      float l = s_lpart[k & 1][r0][row];
+      float l = 0.f;
 #pragma unroll
-      for (int s2 = 1; s2 < kSets; ++s2) l += s_lpart[k & 1][(r0 + s2) % kSets][row];
-      g_item += n;
+      for (int s2 = 0; s2 < kSets; ++s2) l += s_lpart[k & 1][s2][row];
       const float sd = s_sdiag[k & 1][row];
-      const int idk2 = idk1 >= 0 ? item_at(k + 2, ok) : -1;
-      if (!ok) break;
-      if (idk2 >= 0) put_sdiag(k + 2, idk2);  // sets finished item k: both buffers' readers are done
+      if (k + 2 < n_items) put_sdiag(k + 2);  // sets finished item k: both buffers' readers are done
       if (!(ok = mbar_wait_warp(&bars.item_done[k & 1], (k >> 1) & 1, &abort_flag))) break;
       tc_fence_after();
       uint32_t o[DH];
@@ -558,9 +488,6 @@ __global__ void __launch_bounds__(kMainThreads, 1)
         lse[(size_t)bh * S + qrow] =
             bad ? __int_as_float(0x7FC00000) : (sd * c + kRefShift + __log2f(l)) * 0.6931471805599453f;
       }
-      item_release(k);
-      idk = idk1;
-      idk1 = idk2;
     }
     tc_fence_before();
   } else {
@@ -575,13 +502,10 @@ __global__ void __launch_bounds__(kMainThreads, 1)
     const float2 c2 = make_float2(c, c);
     bool ok = true;
     int g = 0;  // global tile index at the start of the current item
-    int idk = item_at(0, ok);
-    int n_next = idk >= 0 ? item_ntiles(idk) : 0;
-    for (int k = 0; ok && idk >= 0; ++k) {
+    int n_next = n_items > 0 ? item_ntiles(item_id(0)) : 0;
+    for (int k = 0; ok && k < n_items; ++k) {
       const int n = n_next;
-      const int idk1 = item_at(k + 1, ok);
-      if (!ok) break;
-      n_next = idk1 >= 0 ? item_ntiles(idk1) : 0;
+      n_next = k + 1 < n_items ? item_ntiles(item_id(k + 1)) : 0;
       if (!(ok = mbar_wait_warp(&bars.sdiag_full[k & 1], (k >> 1) & 1, &abort_flag))) break;
       const float nref = -(s_sdiag[k & 1][row] * c + kRefShift);
       const float2 nm2 = make_float2(nref, nref);
@@ -639,8 +563,6 @@ __global__ void __launch_bounds__(kMainThreads, 1)
       g += n;
       s_lpart[k & 1][set][row] = (lsum[0].x + lsum[0].y) + (lsum[1].x + lsum[1].y);
       mbar_arrive_warp(&bars.lsum_full[k & 1]);
-      item_release(k);
-      idk = idk1;
     }
     tc_fence_before();
   }
@@ -654,7 +576,7 @@ __global__ void __launch_bounds__(kMainThreads, 1)
 
 template <int DH>
 int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, float scale,
-           const rt_tile_plan& plan, uint16_t* o, float* lse, int* work_counter, cudaStream_t stream) {
+           const rt_tile_plan& plan, uint16_t* o, float* lse, cudaStream_t stream) {
   using M = MainCfg<DH>;
   CUtensorMap tq, tk, tv;
   if (make_qkv_tensor_map(&tq, q, B * H, S, DH) != RT_OK || make_qkv_tensor_map(&tk, k, B * H, S, DH) != RT_OK ||
@@ -676,12 +598,7 @@ int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H
   const int sms = dev >= 0 && dev < 64 ? num_sms[dev] : 148;
   const long long items = (long long)B * H * plan.tiles;
   const int grid = (int)std::min<long long>(items, sms);
-  if (work_counter != nullptr) {  // items are taken from the counter in order, starting at 0
-    const cudaError_t e = cudaMemsetAsync(work_counter, 0, sizeof(int), stream);
-    if (e != cudaSuccess) return cuda_failure(e, "cudaMemsetAsync(work counter)");
-  }
-  attn_fwd_kernel<DH><<<grid, kMainThreads, M::kDynSmem, stream>>>(tq, tk, tv, q, k, plan, H, S, scale_log2, o, lse,
-                                                                   work_counter);
+  attn_fwd_kernel<DH><<<grid, kMainThreads, M::kDynSmem, stream>>>(tq, tk, tv, q, k, plan, H, S, scale_log2, o, lse);
   if (int st = check_launch("attn_fwd_kernel launch")) return st;
   const long long rows = (long long)B * H * S;
   const int fix_blocks = (int)std::min<long long>((rows + 255) / 256, 4LL * (dev >= 0 && dev < 64 ? num_sms[dev] : 148));
@@ -692,10 +609,9 @@ int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H
 }  // namespace fwd
 
 int launch_attention_fwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, int Dh,
-                         float scale, const rt_tile_plan& plan, uint16_t* o, float* lse, int* work_counter,
-                         cudaStream_t stream) {
-  if (Dh == 64) return fwd::launch<64>(q, k, v, B, H, S, scale, plan, o, lse, work_counter, stream);
-  if (Dh == 32) return fwd::launch<32>(q, k, v, B, H, S, scale, plan, o, lse, work_counter, stream);
+                         float scale, const rt_tile_plan& plan, uint16_t* o, float* lse, cudaStream_t stream) {
+  if (Dh == 64) return fwd::launch<64>(q, k, v, B, H, S, scale, plan, o, lse, stream);
+  if (Dh == 32) return fwd::launch<32>(q, k, v, B, H, S, scale, plan, o, lse, stream);
   return RT_ERR_UNSUPPORTED;
 }
 

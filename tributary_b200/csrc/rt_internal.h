@@ -22,7 +22,7 @@ int launch_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids, co
 
 int launch_attention_fwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S,
                          int Dh, float scale, const rt_tile_plan& plan, uint16_t* o, float* lse,
-                         int* work_counter, cudaStream_t stream);
+                         cudaStream_t stream);
 
 int launch_attention_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* o,
                          const uint16_t* d_o, const float* lse, int B, int H, int S, int Dh,

@@ -46,13 +46,20 @@ __global__ void fk_pack_kernel(const uint8_t* __restrict__ fk_adj, int R, int WR
 
 // flags[b] = 1 when min(perm[b][.], S-1) is a permutation of [0, S): then
 // p_i == p_j only for i == j, and the diagonal term of the element rule is
-// the identity. One CTA per sample marks each value in a shared bitmap.
+// the identity. One CTA per sample marks each value in a shared bitmap. It
+// also clears the sample's live / fully-live bitmap words (tw = T * W of
+// them), which tile_mask_kernel then sets with atomic ORs.
 __global__ void __launch_bounds__(1024) perm_check_kernel(const uint16_t* __restrict__ perm, int S,
-                                                           int32_t* __restrict__ flags) {
+                                                           int32_t* __restrict__ flags, uint32_t* __restrict__ live,
+                                                           uint32_t* __restrict__ full, int tw) {
   __shared__ uint32_t bm[65536 / 32];
   __shared__ int dup;
   const int b = blockIdx.x;
   const int words = (S + 31) / 32;
+  for (int w = threadIdx.x; w < tw; w += blockDim.x) {
+    live[(size_t)b * tw + w] = 0u;
+    full[(size_t)b * tw + w] = 0u;
+  }
   for (int w = threadIdx.x; w < words; w += blockDim.x) bm[w] = 0u;
   if (threadIdx.x == 0) dup = 0;
   __syncthreads();
@@ -320,16 +327,13 @@ int launch_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids, co
   const int T = plan.tiles;
   const int W = plan.words;
   const int WR = (R + 31) / 32;
-  cudaError_t e = cudaMemsetAsync(plan.live_bits, 0, sizeof(uint32_t) * (size_t)B * T * W, stream);
-  if (e == cudaSuccess) e = cudaMemsetAsync(plan.full_bits, 0, sizeof(uint32_t) * (size_t)B * T * W, stream);
-  if (e != cudaSuccess) return cuda_failure(e, "cudaMemsetAsync(tile bitmaps)");
   const uint32_t* fk_bits = nullptr;
   if ((kind == RT_MASK_FEATURE || kind == RT_MASK_NEIGHBOR) && R > 0) {
     fk_pack_kernel<<<dim3(R, B), 32, 0, stream>>>(fk_adj, R, WR, kind == RT_MASK_NEIGHBOR ? 1 : 0,
                                                   plan.fk_bits);
     fk_bits = plan.fk_bits;
   }
-  perm_check_kernel<<<B, 1024, 0, stream>>>(perm, S, plan.nnz + 1);
+  perm_check_kernel<<<B, 1024, 0, stream>>>(perm, S, plan.nnz + 1, plan.live_bits, plan.full_bits, T * W);
   const dim3 grid((T + kKeyTilesPerCta - 1) / kKeyTilesPerCta, T, B);
   const bool staged = WR <= kMaxStagedWords;
   const size_t fk_smem = sizeof(uint32_t) * RT_TILE * (size_t)(WR | 1);
