@@ -72,156 +72,191 @@ __global__ void __launch_bounds__(1024) perm_check_kernel(const uint16_t* __rest
   if (threadIdx.x == 0) flags[b] = dup ? 0 : 1;
 }
 
-constexpr int kKeyTilesPerCta = 8;
+constexpr int kTileWarps = 8;  // key tiles per CTA, one per warp
 constexpr int kMaxStagedWords = 64;
 
-// One CTA per (b, q-tile, run of kKeyTilesPerCta key tiles); thread = query
-// row. For each key tile the keys are grouped inside each warp by the value
-// the relation compares -- row id (feature, neighbor) or column id (column) --
-// with __match_any_sync, giving per warp a table of (value, 32-bit key set).
-// In the sampler's cell orders a tile holds runs of one row or column, so a
-// table has a handful of entries, and a query evaluates its 128 key bits as
-// the OR of the key sets whose value its relation admits (one test per
-// group instead of one per key), ANDed with the keys' validity. The feature /
-// neighbor relation tests bit `value` of the query row's packed fk row, staged
-// in shared memory once per CTA (odd row stride: conflict-free) when it has at
-// most kMaxStagedWords words. The diagonal term p_i == p_j is i == j for
-// samples whose perm is a permutation (flags from perm_check_kernel) and is
-// tested key by key otherwise.
+// 32 x 32 bit transpose across a warp: lane l holds row l on entry and
+// column l on exit (bit c of the result = bit l of lane c's row). Five
+// butterfly steps; step j swaps the off-diagonal j x j blocks of each
+// 2j x 2j block between lanes l and l ^ j.
+__device__ __forceinline__ uint32_t warp_transpose32(uint32_t x, int lane) {
+  constexpr uint32_t kMask[5] = {0x0000FFFFu, 0x00FF00FFu, 0x0F0F0F0Fu, 0x33333333u, 0x55555555u};
+#pragma unroll
+  for (int s = 0; s < 5; ++s) {
+    const int j = 16 >> s;
+    const uint32_t m = kMask[s];
+    const uint32_t y = __shfl_xor_sync(0xFFFFFFFFu, x, j);
+    x = (lane & j) ? ((x & ~m) | ((y & ~m) >> j)) : ((x & m) | ((y & m) << j));
+  }
+  return x;
+}
+
+// One CTA per (b, q-tile, run of kTileWarps key tiles); each warp evaluates
+// one key tile on its own, without block barriers, so the gathers of several
+// tiles are in flight at once. Lane l holds queries 32 m + l (m = 0..3) of
+// the q-tile and, per 32-key word of its key tile, key 32 kw + l. The keys of
+// a word are grouped by the value the relation compares -- row id (feature,
+// neighbor) or column id (column) -- with __match_any_sync; in the sampler's
+// cell orders a word holds runs of one row or column, so there are few groups,
+// and a query evaluates its 32 key bits as the OR of the key sets whose value
+// its relation admits (one test per group instead of one per key), ANDed with
+// the keys' validity. The feature / neighbor relation tests bit `value` of the
+// query row's packed fk row, staged in shared memory once per CTA (odd row
+// stride: conflict-free) when it has at most kMaxStagedWords words. The
+// diagonal term p_i == p_j is i == j for samples whose perm is a permutation
+// (flags from perm_check_kernel) and is tested key by key otherwise.
 template <int KIND, bool kStaged>
-__global__ void __launch_bounds__(128) tile_mask_kernel(
+__global__ void __launch_bounds__(kTileWarps * 32) tile_mask_kernel(
     const uint16_t* __restrict__ perm, const uint16_t* __restrict__ seq_row_ids,
     const int32_t* __restrict__ column_ids, const uint8_t* __restrict__ is_padding,
     const uint32_t* __restrict__ fk_bits, int S, int R, int WR, rt_tile_plan plan) {
   constexpr bool kFk = KIND == RT_MASK_FEATURE || KIND == RT_MASK_NEIGHBOR;
+  constexpr uint32_t kAll = 0xFFFFFFFFu;
   const int qt = blockIdx.y;
   const int b = blockIdx.z;
   const int T = plan.tiles;
-  const int kt_begin = blockIdx.x * kKeyTilesPerCta;
-  const int kt_end = min(T, kt_begin + kKeyTilesPerCta);
-  const int t = threadIdx.x;
-  const int lane = t & 31;
-  const int warp = t >> 5;
-
-  __shared__ int s_korig[RT_TILE];
-  __shared__ uint32_t s_valid[4];
-  __shared__ int s_gkey[4][32];
-  __shared__ uint32_t s_gbits[4][32];
-  __shared__ int s_gcount[4];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int kt = blockIdx.x * kTileWarps + warp;
   extern __shared__ uint32_t s_fk[];  // [128][WR | 1] when kStaged
-
   const size_t boff = (size_t)b * S;
-  const int i = qt * RT_TILE + t;
-  const bool qin = i < S;
-  int pi = -2, ri = 0, ci = 0;
-  bool padi = true;
-  if (qin) {
-    pi = min((int)perm[boff + i], S - 1);
-    ri = seq_row_ids[boff + pi];
-    if (R > 0 && ri > R - 1) ri = R - 1;
-    ci = column_ids[boff + pi];
-    padi = is_padding[boff + pi] != 0;
-  }
-  const bool perm_ok = plan.nnz[1 + b] != 0;
-  const uint32_t* fkrow = (kFk && R > 0 && fk_bits != nullptr) ? fk_bits + ((size_t)b * R + ri) * WR : nullptr;
   const int fk_stride = WR | 1;
-  if (kStaged && fkrow != nullptr)
-    for (int w = 0; w < WR; ++w) s_fk[t * fk_stride + w] = __ldg(fkrow + w);
-  auto fk_bit = [&](int r) -> bool {
-    if (fkrow == nullptr) return false;
-    const uint32_t word = kStaged ? s_fk[t * fk_stride + (r >> 5)] : __ldg(fkrow + (r >> 5));
+  const bool have_fk = kFk && R > 0 && fk_bits != nullptr;
+
+  // this lane's queries 32 m + lane (every warp holds the same ones)
+  int pi[4], ri[4], ci[4];
+  bool qin[4], act[4];
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    const int i = qt * RT_TILE + 32 * m + lane;
+    qin[m] = i < S;
+    pi[m] = -2;
+    ri[m] = 0;
+    ci[m] = 0;
+    bool pad = true;
+    if (qin[m]) {
+      pi[m] = min((int)perm[boff + i], S - 1);
+      int r = seq_row_ids[boff + pi[m]];
+      if (R > 0 && r > R - 1) r = R - 1;
+      ri[m] = r;
+      ci[m] = column_ids[boff + pi[m]];
+      pad = is_padding[boff + pi[m]] != 0;
+    }
+    act[m] = qin[m] && !pad;
+  }
+  if (kStaged && have_fk) {
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const uint32_t* row = fk_bits + ((size_t)b * R + ri[m]) * WR;
+      for (int w = warp; w < WR; w += kTileWarps) s_fk[(32 * m + lane) * fk_stride + w] = __ldg(row + w);
+    }
+    __syncthreads();
+  }
+  if (kt >= T) return;  // warp-uniform, after the only block barrier
+  auto fk_bit = [&](int m, int r) -> bool {
+    if (!have_fk) return false;
+    const uint32_t word = kStaged ? s_fk[(32 * m + lane) * fk_stride + (r >> 5)]
+                                  : __ldg(fk_bits + ((size_t)b * R + ri[m]) * WR + (r >> 5));
     return (word >> (r & 31)) & 1u;
   };
 
-  for (int kt = kt_begin; kt < kt_end; ++kt) {
-    {  // key metadata: validity bits, diagonal candidates and the warp's group table
-      const int j = kt * RT_TILE + t;
-      const bool jin = j < S;
-      int pj = -1, rj = 0, cj = 0;
-      bool padj = true;
-      if (jin) {
-        pj = min((int)perm[boff + j], S - 1);  // out-of-range perm entries clamp
-        rj = seq_row_ids[boff + pj];
-        if (R > 0 && rj > R - 1) rj = R - 1;
-        cj = column_ids[boff + pj];
-        padj = is_padding[boff + pj] != 0;
-      }
-      s_korig[t] = pj;
-      const uint32_t vb = __ballot_sync(0xFFFFFFFFu, jin && !padj);
-      if (lane == 0) s_valid[warp] = vb;
-      if (KIND != RT_MASK_FULL) {
-        const int gk = KIND == RT_MASK_COLUMN ? cj : rj;
-        const uint32_t same = __match_any_sync(0xFFFFFFFFu, gk);
-        const bool leader = (__ffs(same) - 1) == lane;
-        const uint32_t lb = __ballot_sync(0xFFFFFFFFu, leader);
-        if (leader) {
-          const int g = __popc(lb & ((1u << lane) - 1u));
-          s_gkey[warp][g] = gk;
-          s_gbits[warp][g] = same;
-        }
-        if (lane == 0) s_gcount[warp] = __popc(lb);
-      }
-    }
-    __syncthreads();
-
-    uint32_t w4[4] = {0u, 0u, 0u, 0u};
-    if (qin && !padi) {
+  // key metadata of the tile's four words: lane holds key kt * 128 + 32 kw + lane
+  int pj[4], gk[4];
+  uint32_t valid[4];
 #pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        uint32_t rel = 0u;
-        if (KIND == RT_MASK_FULL) {
-          rel = 0xFFFFFFFFu;
-        } else {
-          const int n = s_gcount[w];
-          for (int g = 0; g < n; ++g) {
-            const int key = s_gkey[w][g];
-            bool r;
-            if (KIND == RT_MASK_COLUMN) r = ci == key;
-            else if (KIND == RT_MASK_FEATURE) r = ri == key || fk_bit(key);
-            else r = fk_bit(key);
-            if (r) rel |= s_gbits[w][g];
-          }
-        }
-        w4[w] = rel & s_valid[w];
-      }
+  for (int kw = 0; kw < 4; ++kw) {
+    const int j = kt * RT_TILE + 32 * kw + lane;
+    const bool jin = j < S;
+    int p = -1, r = 0, c = 0;
+    bool pad = true;
+    if (jin) {
+      p = min((int)perm[boff + j], S - 1);  // out-of-range perm entries clamp
+      r = seq_row_ids[boff + p];
+      if (R > 0 && r > R - 1) r = R - 1;
+      c = column_ids[boff + p];
+      pad = is_padding[boff + p] != 0;
     }
-    if (qin) {
-      if (perm_ok) {
-        if (kt == qt) w4[warp] |= 1u << lane;  // p_i == p_j exactly when i == j
-      } else {
-#pragma unroll 8
-        for (int u = 0; u < RT_TILE; ++u)
-          if (s_korig[u] == pi) w4[u >> 5] |= 1u << (u & 31);
-      }
-    }
-
-    const int any = __syncthreads_or((w4[0] | w4[1] | w4[2] | w4[3]) != 0u);
-    const int all = __syncthreads_and(qin && (w4[0] & w4[1] & w4[2] & w4[3]) == 0xFFFFFFFFu);
-    if (!any) continue;  // block-uniform; the barriers above end every read of this tile's tables
-    const size_t tile_q = ((size_t)b * T + qt) * T + kt;
-    const size_t tile_k = ((size_t)b * T + kt) * T + qt;
-    if (t == 0) {
-      const size_t wi = ((size_t)b * T + qt) * plan.words + (kt >> 5);
-      atomicOr(plan.live_bits + wi, 1u << (kt & 31));
-      if (all) atomicOr(plan.full_bits + wi, 1u << (kt & 31));
-    }
-    if (all) continue;  // block-uniform
-    reinterpret_cast<uint4*>(plan.tile_masks)[tile_q * RT_TILE + t] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-    // Transpose 128x128 bits: for key j, this warp's 32 queries form word `warp`
-    // of key j's row in the key-major copy.
-    uint32_t tw[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-#pragma unroll 8
-      for (int u = 0; u < 32; ++u) {
-        const uint32_t bal = __ballot_sync(0xFFFFFFFFu, (w4[w] >> u) & 1u);
-        if (lane == u) tw[w] = bal;
-      }
-    }
-    uint32_t* dst = plan.tile_masks_t + tile_k * RT_TILE * 4;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) dst[(size_t)(w * 32 + lane) * 4 + warp] = tw[w];
+    pj[kw] = p;
+    gk[kw] = KIND == RT_MASK_COLUMN ? c : r;
+    valid[kw] = __ballot_sync(kAll, jin && !pad);
   }
+
+  uint32_t w[4][4];  // [query block m][key word kw]: this lane's query row, 32 keys
+#pragma unroll
+  for (int kw = 0; kw < 4; ++kw) {
+    uint32_t rel[4] = {0u, 0u, 0u, 0u};
+    if (KIND == RT_MASK_FULL) {
+#pragma unroll
+      for (int m = 0; m < 4; ++m) rel[m] = kAll;
+    } else {
+      const uint32_t same = __match_any_sync(kAll, gk[kw]);
+      uint32_t leaders = __ballot_sync(kAll, (__ffs(same) - 1) == lane);
+      while (leaders) {  // warp-uniform
+        const int src = __ffs(leaders) - 1;
+        leaders &= leaders - 1u;
+        const int key = __shfl_sync(kAll, gk[kw], src);
+        const uint32_t bits = __shfl_sync(kAll, same, src);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          bool r;
+          if (KIND == RT_MASK_COLUMN) r = ci[m] == key;
+          else if (KIND == RT_MASK_FEATURE) r = ri[m] == key || fk_bit(m, key);
+          else r = fk_bit(m, key);
+          if (r) rel[m] |= bits;
+        }
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < 4; ++m) w[m][kw] = act[m] ? (rel[m] & valid[kw]) : 0u;
+  }
+  if (plan.nnz[1 + b] != 0) {  // perm is a permutation: p_i == p_j exactly when i == j
+    if (kt == qt) {
+#pragma unroll
+      for (int m = 0; m < 4; ++m)
+        if (qin[m]) w[m][m] |= 1u << lane;
+    }
+  } else {
+#pragma unroll
+    for (int kw = 0; kw < 4; ++kw) {
+      for (int u = 0; u < 32; ++u) {
+        const int p = __shfl_sync(kAll, pj[kw], u);
+#pragma unroll
+        for (int m = 0; m < 4; ++m)
+          if (p == pi[m]) w[m][kw] |= 1u << u;  // pi = -2 for queries past S, pj = -1 for keys past S
+      }
+    }
+  }
+
+  uint32_t any_v = 0u, all_v = kAll;
+  bool rows_in = true;
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    rows_in = rows_in && qin[m];
+#pragma unroll
+    for (int kw = 0; kw < 4; ++kw) {
+      any_v |= w[m][kw];
+      all_v &= w[m][kw];
+    }
+  }
+  if (!__any_sync(kAll, any_v != 0u)) return;  // warp-uniform
+  const bool all = __all_sync(kAll, rows_in && all_v == kAll);
+  if (lane == 0) {
+    const size_t wi = ((size_t)b * T + qt) * plan.words + (kt >> 5);
+    atomicOr(plan.live_bits + wi, 1u << (kt & 31));
+    if (all) atomicOr(plan.full_bits + wi, 1u << (kt & 31));
+  }
+  if (all) return;  // warp-uniform
+  const size_t tile_q = ((size_t)b * T + qt) * T + kt;
+  const size_t tile_k = ((size_t)b * T + kt) * T + qt;
+  uint4* dst_q = reinterpret_cast<uint4*>(plan.tile_masks) + tile_q * RT_TILE;
+#pragma unroll
+  for (int m = 0; m < 4; ++m) dst_q[32 * m + lane] = make_uint4(w[m][0], w[m][1], w[m][2], w[m][3]);
+  // key-major copy: key 32 kw + lane, its bits over query block m
+  uint4* dst_k = reinterpret_cast<uint4*>(plan.tile_masks_t) + tile_k * RT_TILE;
+#pragma unroll
+  for (int kw = 0; kw < 4; ++kw)
+    dst_k[32 * kw + lane] = make_uint4(warp_transpose32(w[0][kw], lane), warp_transpose32(w[1][kw], lane),
+                                       warp_transpose32(w[2][kw], lane), warp_transpose32(w[3][kw], lane));
 }
 
 // Single block: CSR lists (q2k over (b,qt) rows, k2q over (b,kt) rows) from the bitmaps.
@@ -334,26 +369,26 @@ int launch_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids, co
     fk_bits = plan.fk_bits;
   }
   perm_check_kernel<<<B, 1024, 0, stream>>>(perm, S, plan.nnz + 1, plan.live_bits, plan.full_bits, T * W);
-  const dim3 grid((T + kKeyTilesPerCta - 1) / kKeyTilesPerCta, T, B);
+  const dim3 grid((T + kTileWarps - 1) / kTileWarps, T, B);
   const bool staged = WR <= kMaxStagedWords;
   const size_t fk_smem = sizeof(uint32_t) * RT_TILE * (size_t)(WR | 1);
   if (kind == RT_MASK_COLUMN)
-    tile_mask_kernel<RT_MASK_COLUMN, false><<<grid, RT_TILE, 0, stream>>>(perm, seq_row_ids, column_ids,
+    tile_mask_kernel<RT_MASK_COLUMN, false><<<grid, kTileWarps * 32, 0, stream>>>(perm, seq_row_ids, column_ids,
                                                                           is_padding, fk_bits, S, R, WR, plan);
   else if (kind == RT_MASK_FEATURE && staged)
-    tile_mask_kernel<RT_MASK_FEATURE, true><<<grid, RT_TILE, fk_smem, stream>>>(perm, seq_row_ids, column_ids,
+    tile_mask_kernel<RT_MASK_FEATURE, true><<<grid, kTileWarps * 32, fk_smem, stream>>>(perm, seq_row_ids, column_ids,
                                                                                 is_padding, fk_bits, S, R, WR, plan);
   else if (kind == RT_MASK_FEATURE)
-    tile_mask_kernel<RT_MASK_FEATURE, false><<<grid, RT_TILE, 0, stream>>>(perm, seq_row_ids, column_ids,
+    tile_mask_kernel<RT_MASK_FEATURE, false><<<grid, kTileWarps * 32, 0, stream>>>(perm, seq_row_ids, column_ids,
                                                                            is_padding, fk_bits, S, R, WR, plan);
   else if (kind == RT_MASK_NEIGHBOR && staged)
-    tile_mask_kernel<RT_MASK_NEIGHBOR, true><<<grid, RT_TILE, fk_smem, stream>>>(perm, seq_row_ids, column_ids,
+    tile_mask_kernel<RT_MASK_NEIGHBOR, true><<<grid, kTileWarps * 32, fk_smem, stream>>>(perm, seq_row_ids, column_ids,
                                                                                  is_padding, fk_bits, S, R, WR, plan);
   else if (kind == RT_MASK_NEIGHBOR)
-    tile_mask_kernel<RT_MASK_NEIGHBOR, false><<<grid, RT_TILE, 0, stream>>>(perm, seq_row_ids, column_ids,
+    tile_mask_kernel<RT_MASK_NEIGHBOR, false><<<grid, kTileWarps * 32, 0, stream>>>(perm, seq_row_ids, column_ids,
                                                                             is_padding, fk_bits, S, R, WR, plan);
   else
-    tile_mask_kernel<RT_MASK_FULL, false><<<grid, RT_TILE, 0, stream>>>(perm, seq_row_ids, column_ids,
+    tile_mask_kernel<RT_MASK_FULL, false><<<grid, kTileWarps * 32, 0, stream>>>(perm, seq_row_ids, column_ids,
                                                                         is_padding, fk_bits, S, R, WR, plan);
   {
     const size_t bits_bytes = 2 * sizeof(uint32_t) * (size_t)B * plan.tiles * plan.words;
