@@ -182,9 +182,9 @@ class Workload:
         self.tiles = self.kinds[0]["plan"].tiles
 
     def launches_per_step(self):
-        # prepass: fk pack (feature / neighbor only), tile mask, tile list;
-        # forward: main kernel + row fix-up; backward: row stats, dK/dV, dQ
-        return sum((3 if k in (1, 2) else 2) + 2 + 3 for k in range(4))
+        # prepass: set-up (perm check, fk packing), tile mask, tile list;
+        # forward: main kernel + row fix-up; backward: row stats, dK/dV/dQ, dQ conversion
+        return sum(3 + 2 + 3 for _ in range(4))
 
     def rebuild_plan(self, k):
         lib = self.rt._lib

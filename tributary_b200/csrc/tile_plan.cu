@@ -25,51 +25,67 @@
 
 namespace rt {
 
-// fk_bits[b][r][w] bit t = FEATURE: fk_adj[b][r][32w+t]; NEIGHBOR: fk_adj[b][32w+t][r]
-__global__ void fk_pack_kernel(const uint8_t* __restrict__ fk_adj, int R, int WR, int transpose,
-                               uint32_t* __restrict__ fk_bits) {
-  const int b = blockIdx.y;
-  const int r = blockIdx.x;
-  const uint8_t* base = fk_adj + (size_t)b * R * R;
-  for (int w = threadIdx.x; w < WR; w += blockDim.x) {
-    uint32_t word = 0;
-    for (int t = 0; t < 32; ++t) {
-      const int c = w * 32 + t;
-      if (c < R) {
-        const uint8_t v = transpose ? base[(size_t)c * R + r] : base[(size_t)r * R + c];
-        word |= (v != 0 ? 1u : 0u) << t;
-      }
-    }
-    fk_bits[((size_t)b * R + r) * WR + w] = word;
-  }
-}
+constexpr int kSetupThreads = 1024;
 
-// flags[b] = 1 when min(perm[b][.], S-1) is a permutation of [0, S): then
-// p_i == p_j only for i == j, and the diagonal term of the element rule is
-// the identity. One CTA per sample marks each value in a shared bitmap. It
-// also clears the sample's live / fully-live bitmap words (tw = T * W of
-// them), which tile_mask_kernel then sets with atomic ORs.
-__global__ void __launch_bounds__(1024) perm_check_kernel(const uint16_t* __restrict__ perm, int S,
-                                                           int32_t* __restrict__ flags, uint32_t* __restrict__ live,
-                                                           uint32_t* __restrict__ full, int tw) {
-  __shared__ uint32_t bm[65536 / 32];
-  __shared__ int dup;
-  const int b = blockIdx.x;
-  const int words = (S + 31) / 32;
-  for (int w = threadIdx.x; w < tw; w += blockDim.x) {
-    live[(size_t)b * tw + w] = 0u;
-    full[(size_t)b * tw + w] = 0u;
+__device__ __forceinline__ uint32_t warp_transpose32(uint32_t x, int lane);
+
+// Set-up before the tile masks, one launch:
+// - blocks [0, B): flags[b] = 1 when min(perm[b][.], S-1) is a permutation of
+//   [0, S): then p_i == p_j only for i == j, and the diagonal term of the
+//   element rule is the identity. The block marks each value in a shared
+//   bitmap. It also clears the sample's live / fully-live bitmap words (tw =
+//   T * W of them), which tile_mask_kernel then sets with atomic ORs.
+// - the blocks after them (feature / neighbor kinds): fk_bits[b][r][w] bit t =
+//   FEATURE: fk_adj[b][r][32w+t]; NEIGHBOR: fk_adj[b][32w+t][r]. A warp packs
+//   one 32 x 32 block of fk_adj: per row, 32 lanes read 32 consecutive bytes
+//   and a ballot gives the row's word; the neighbor orientation transposes
+//   the 32 words across the warp.
+__global__ void __launch_bounds__(kSetupThreads) plan_setup_kernel(
+    const uint16_t* __restrict__ perm, int B, int S, int32_t* __restrict__ flags, uint32_t* __restrict__ live,
+    uint32_t* __restrict__ full, int tw, const uint8_t* __restrict__ fk_adj, int R, int WR, int transpose,
+    uint32_t* __restrict__ fk_bits) {
+  if ((int)blockIdx.x < B) {
+    __shared__ uint32_t bm[65536 / 32];
+    __shared__ int dup;
+    const int b = blockIdx.x;
+    const int words = (S + 31) / 32;
+    for (int w = threadIdx.x; w < tw; w += blockDim.x) {
+      live[(size_t)b * tw + w] = 0u;
+      full[(size_t)b * tw + w] = 0u;
+    }
+    for (int w = threadIdx.x; w < words; w += blockDim.x) bm[w] = 0u;
+    if (threadIdx.x == 0) dup = 0;
+    __syncthreads();
+    for (int x = threadIdx.x; x < S; x += blockDim.x) {
+      const int p = min((int)perm[(size_t)b * S + x], S - 1);
+      const uint32_t bit = 1u << (p & 31);
+      if (atomicOr(&bm[p >> 5], bit) & bit) dup = 1;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) flags[b] = dup ? 0 : 1;
+    return;
   }
-  for (int w = threadIdx.x; w < words; w += blockDim.x) bm[w] = 0u;
-  if (threadIdx.x == 0) dup = 0;
-  __syncthreads();
-  for (int x = threadIdx.x; x < S; x += blockDim.x) {
-    const int p = min((int)perm[(size_t)b * S + x], S - 1);
-    const uint32_t bit = 1u << (p & 31);
-    if (atomicOr(&bm[p >> 5], bit) & bit) dup = 1;
+  const int lane = threadIdx.x & 31;
+  const long long task = (long long)(blockIdx.x - B) * (kSetupThreads / 32) + (threadIdx.x >> 5);
+  const long long per_b = (long long)WR * WR;  // 32 x 32 blocks of one sample
+  if (task >= per_b * B) return;  // warp-uniform
+  const int b = (int)(task / per_b);
+  const int rb = (int)((task % per_b) / WR), cb = (int)(task % WR);
+  const uint8_t* base = fk_adj + (size_t)b * R * R;
+  const int col = cb * 32 + lane;
+  uint32_t mine = 0u;  // lane t: row 32 rb + t, columns [32 cb, +32)
+  for (int t = 0; t < 32; ++t) {
+    const int row = rb * 32 + t;
+    const bool v = row < R && col < R && base[(size_t)row * R + col] != 0;
+    const uint32_t bal = __ballot_sync(0xFFFFFFFFu, v);
+    if (lane == t) mine = bal;
   }
-  __syncthreads();
-  if (threadIdx.x == 0) flags[b] = dup ? 0 : 1;
+  if (!transpose) {
+    if (rb * 32 + lane < R) fk_bits[((size_t)b * R + rb * 32 + lane) * WR + cb] = mine;
+  } else {
+    const uint32_t x = warp_transpose32(mine, lane);  // lane c: rows [32 rb, +32) of column 32 cb + c
+    if (col < R) fk_bits[((size_t)b * R + col) * WR + rb] = x;
+  }
 }
 
 constexpr int kTileWarps = 8;  // key tiles per CTA, one per warp
@@ -104,7 +120,7 @@ __device__ __forceinline__ uint32_t warp_transpose32(uint32_t x, int lane) {
 // query row's packed fk row, staged in shared memory once per CTA (odd row
 // stride: conflict-free) when it has at most kMaxStagedWords words. The
 // diagonal term p_i == p_j is i == j for samples whose perm is a permutation
-// (flags from perm_check_kernel) and is tested key by key otherwise.
+// (flags from plan_setup_kernel) and is tested key by key otherwise.
 template <int KIND, bool kStaged>
 __global__ void __launch_bounds__(kTileWarps * 32) tile_mask_kernel(
     const uint16_t* __restrict__ perm, const uint16_t* __restrict__ seq_row_ids,
@@ -259,100 +275,113 @@ __global__ void __launch_bounds__(kTileWarps * 32) tile_mask_kernel(
                                        warp_transpose32(w[2][kw], lane), warp_transpose32(w[3][kw], lane));
 }
 
-// Single block: CSR lists (q2k over (b,qt) rows, k2q over (b,kt) rows) from the bitmaps.
-constexpr int kListSmemBytes = 96 * 1024;  // tile_list_kernel's staged bitmaps
+// CSR lists (q2k over (b,qt) rows, k2q over (b,kt) rows) from the bitmaps, one
+// block per sample. Both lists of sample b start at the number of live tiles
+// of the samples before it, which the block counts from their bitmaps; the
+// sample's own bitmaps are staged in shared memory when they fit.
+constexpr int kListSmemBytes = 96 * 1024;  // tile_list_kernel's staged bitmaps of one sample
+constexpr int kListThreads = 512;
 
-__global__ void __launch_bounds__(1024) tile_list_kernel(rt_tile_plan plan) {
+__global__ void __launch_bounds__(kListThreads) tile_list_kernel(rt_tile_plan plan) {
   const int T = plan.tiles;
   const int W = plan.words;
-  const int nrows = plan.batch * T;
-  const int nthreads = blockDim.x;
-  const int chunk = (nrows + nthreads - 1) / nthreads;
-  const int r0 = min(nrows, (int)threadIdx.x * chunk);
-  const int r1 = min(nrows, r0 + chunk);
-  __shared__ int s_warp[32];
+  const int b = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int kWarps = kListThreads / 32;
+  __shared__ int s_warp[kWarps];
   __shared__ int s_total;
-  // the bitmaps (a few KB) in shared memory when they fit: every row and
-  // column scan below reads them many times
   extern __shared__ uint32_t s_bits[];
-  const int nwords = nrows * W;
+  const int nwords = T * W;
   const bool staged = 2LL * nwords * (long long)sizeof(uint32_t) <= (long long)kListSmemBytes;
-  const uint32_t* live = plan.live_bits;
-  const uint32_t* full_b = plan.full_bits;
-  if (staged) {
-    for (int i = threadIdx.x; i < nwords; i += blockDim.x) {
-      s_bits[i] = plan.live_bits[i];
-      s_bits[nwords + i] = plan.full_bits[i];
-    }
-    __syncthreads();
-    live = s_bits;
-    full_b = s_bits + nwords;
-  }
+  const uint32_t* live = plan.live_bits + (size_t)b * nwords;
+  const uint32_t* full_b = plan.full_bits + (size_t)b * nwords;
 
-  for (int pass = 0; pass < 2; ++pass) {
-    const bool by_q = pass == 0;
-    int* ptr = by_q ? plan.q2k_ptr : plan.k2q_ptr;
-    int* idx = by_q ? plan.q2k_idx : plan.k2q_idx;
-    int local = 0;
-    for (int r = r0; r < r1; ++r) {
-      const int b = r / T, x = r % T;
-      if (by_q) {
-        for (int w = 0; w < W; ++w) local += __popc(live[((size_t)b * T + x) * W + w]);
-      } else {
-        for (int q = 0; q < T; ++q)
-          local += (live[((size_t)b * T + q) * W + (x >> 5)] >> (x & 31)) & 1u;
-      }
-    }
-    // exclusive block scan of `local`
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int incl = local;
+  // exclusive block scan of one value per thread; returns the prefix, leaves the sum in s_total
+  auto block_scan = [&](int v) {
+    int incl = v;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-      if (lane >= o) incl += v;
+      const int u = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += u;
     }
     if (lane == 31) s_warp[warp] = incl;
     __syncthreads();
     if (warp == 0) {
-      const int nw = (nthreads + 31) >> 5;
-      int v = lane < nw ? s_warp[lane] : 0;
-      int vi = v;
+      const int x = lane < kWarps ? s_warp[lane] : 0;
+      int xi = x;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
-        const int u = __shfl_up_sync(0xFFFFFFFFu, vi, o);
-        if (lane >= o) vi += u;
+        const int u = __shfl_up_sync(0xFFFFFFFFu, xi, o);
+        if (lane >= o) xi += u;
       }
-      if (lane < nw) s_warp[lane] = vi - v;
-      if (lane == 31) s_total = vi;
+      if (lane < kWarps) s_warp[lane] = xi - x;
+      if (lane == 31) s_total = xi;
     }
     __syncthreads();
-    int pos = s_warp[warp] + incl - local;
-    for (int r = r0; r < r1; ++r) {
-      const int b = r / T, x = r % T;
-      ptr[r] = pos;
-      if (by_q) {
-        for (int kt = 0; kt < T; ++kt) {
-          const size_t wi = ((size_t)b * T + x) * W + (kt >> 5);
-          if ((live[wi] >> (kt & 31)) & 1u) {
-            const bool full = (full_b[wi] >> (kt & 31)) & 1u;
-            idx[pos++] = kt | (full ? (int)0x80000000u : 0);
-          }
+    const int r = s_warp[warp] + incl - v;
+    return r;
+  };
+
+  // live tiles of the samples before b
+  int before = 0;
+  for (long long i = threadIdx.x; i < (long long)b * nwords; i += kListThreads) before += __popc(plan.live_bits[i]);
+  if (staged) {
+    for (int i = threadIdx.x; i < nwords; i += kListThreads) {
+      s_bits[i] = live[i];
+      s_bits[nwords + i] = full_b[i];
+    }
+    live = s_bits;
+    full_b = s_bits + nwords;
+  }
+  (void)block_scan(before);  // also orders the staging above before the reads below
+  const int base = s_total;
+  __syncthreads();
+
+  // rows x of this sample in chunks of kListThreads; thread = row
+  for (int pass = 0; pass < 2; ++pass) {
+    const bool by_q = pass == 0;
+    int* ptr = by_q ? plan.q2k_ptr : plan.k2q_ptr;
+    int* idx = by_q ? plan.q2k_idx : plan.k2q_idx;
+    int run = base;
+    for (int x0 = 0; x0 < T; x0 += kListThreads) {
+      const int x = x0 + threadIdx.x;
+      int cnt = 0;
+      if (x < T) {
+        if (by_q) {
+          for (int w = 0; w < W; ++w) cnt += __popc(live[x * W + w]);
+        } else {
+          for (int q = 0; q < T; ++q) cnt += (live[q * W + (x >> 5)] >> (x & 31)) & 1u;
         }
-      } else {
-        for (int qt = 0; qt < T; ++qt) {
-          const size_t wi = ((size_t)b * T + qt) * W + (x >> 5);
-          if ((live[wi] >> (x & 31)) & 1u) {
-            const bool full = (full_b[wi] >> (x & 31)) & 1u;
-            idx[pos++] = qt | (full ? (int)0x80000000u : 0);
+      }
+      int pos = run + block_scan(cnt);
+      const int chunk_total = s_total;
+      if (x < T) {
+        ptr[(size_t)b * T + x] = pos;
+        if (by_q) {
+          for (int kt = 0; kt < T; ++kt) {
+            const int wi = x * W + (kt >> 5);
+            if ((live[wi] >> (kt & 31)) & 1u) {
+              const bool f = (full_b[wi] >> (kt & 31)) & 1u;
+              idx[pos++] = kt | (f ? (int)0x80000000u : 0);
+            }
+          }
+        } else {
+          for (int qt = 0; qt < T; ++qt) {
+            const int wi = qt * W + (x >> 5);
+            if ((live[wi] >> (x & 31)) & 1u) {
+              const bool f = (full_b[wi] >> (x & 31)) & 1u;
+              idx[pos++] = qt | (f ? (int)0x80000000u : 0);
+            }
           }
         }
       }
+      run += chunk_total;
+      __syncthreads();  // s_total / s_warp are reused by the next chunk's scan
     }
-    if (threadIdx.x == 0) {
-      ptr[nrows] = s_total;
-      if (by_q) *plan.nnz = s_total;
+    if (b == plan.batch - 1 && threadIdx.x == 0) {
+      ptr[(size_t)plan.batch * T] = run;
+      if (by_q) *plan.nnz = run;
     }
-    __syncthreads();
   }
 }
 
@@ -362,13 +391,13 @@ int launch_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids, co
   const int T = plan.tiles;
   const int W = plan.words;
   const int WR = (R + 31) / 32;
-  const uint32_t* fk_bits = nullptr;
-  if ((kind == RT_MASK_FEATURE || kind == RT_MASK_NEIGHBOR) && R > 0) {
-    fk_pack_kernel<<<dim3(R, B), 32, 0, stream>>>(fk_adj, R, WR, kind == RT_MASK_NEIGHBOR ? 1 : 0,
-                                                  plan.fk_bits);
-    fk_bits = plan.fk_bits;
-  }
-  perm_check_kernel<<<B, 1024, 0, stream>>>(perm, S, plan.nnz + 1, plan.live_bits, plan.full_bits, T * W);
+  const bool needs_fk = (kind == RT_MASK_FEATURE || kind == RT_MASK_NEIGHBOR) && R > 0;
+  const uint32_t* fk_bits = needs_fk ? plan.fk_bits : nullptr;
+  const long long fk_tasks = needs_fk ? (long long)B * WR * WR : 0;
+  const int setup_blocks = B + (int)((fk_tasks + kSetupThreads / 32 - 1) / (kSetupThreads / 32));
+  plan_setup_kernel<<<setup_blocks, kSetupThreads, 0, stream>>>(perm, B, S, plan.nnz + 1, plan.live_bits,
+                                                                plan.full_bits, T * W, fk_adj, R, WR,
+                                                                kind == RT_MASK_NEIGHBOR ? 1 : 0, plan.fk_bits);
   const dim3 grid((T + kTileWarps - 1) / kTileWarps, T, B);
   const bool staged = WR <= kMaxStagedWords;
   const size_t fk_smem = sizeof(uint32_t) * RT_TILE * (size_t)(WR | 1);
@@ -391,7 +420,7 @@ int launch_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids, co
     tile_mask_kernel<RT_MASK_FULL, false><<<grid, kTileWarps * 32, 0, stream>>>(perm, seq_row_ids, column_ids,
                                                                         is_padding, fk_bits, S, R, WR, plan);
   {
-    const size_t bits_bytes = 2 * sizeof(uint32_t) * (size_t)B * plan.tiles * plan.words;
+    const size_t bits_bytes = 2 * sizeof(uint32_t) * (size_t)plan.tiles * plan.words;  // one sample
     const size_t smem = bits_bytes <= (size_t)kListSmemBytes ? bits_bytes : 0;
     static bool list_configured[64] = {false};
     int dev = 0;
@@ -402,7 +431,7 @@ int launch_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids, co
       if (e != cudaSuccess) return cuda_failure(e, "cudaFuncSetAttribute(tile_list_kernel)");
       list_configured[dev] = true;
     }
-    tile_list_kernel<<<1, 1024, smem, stream>>>(plan);
+    tile_list_kernel<<<B, kListThreads, smem, stream>>>(plan);
   }
   return check_launch("tile plan kernels launch");
 }
