@@ -202,8 +202,10 @@ class ValueEncoder(nn.Module):
             self.text(cells["text_vectors"][cells["text_ids"]]),
             torch.zeros_like(col),
         ], dim=2)  # [B, S, 7, D]
-        onehot = F.one_hot(cells["stypes"].long(), NUM_STYPES).to(vals.dtype)
-        raw = torch.einsum("bst,bstd->bsd", onehot, vals)
+        # each cell's own semantic-type slice (the one-hot contraction of the
+        # reference picks exactly this row)
+        sel = cells["stypes"].long().clamp(0, NUM_STYPES - 1)[..., None, None].expand(-1, -1, 1, vals.shape[-1])
+        raw = torch.gather(vals, 2, sel).squeeze(2)
         is_null = cells["is_null"][..., None].to(raw.dtype)
         is_target = cells["is_target"][..., None].to(raw.dtype)
         v = is_null * self.null_emb.to(raw.dtype) + (1 - is_null) * raw
