@@ -190,6 +190,27 @@ int rt_attention_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, co
                      uint16_t* dq, uint16_t* dk, uint16_t* dv, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* Backward of a whole attention sublayer step from the token-order
+ * projection: the gather into the kind's cell order and the QK L2
+ * normalisation with temperature (rt_qk_prepare, layers.py:63-80,139-142)
+ * followed by the attention (layers.py:82-97). Equivalent to rt_attention_bwd
+ * then rt_qk_prepare_bwd, in one pass: the normalisation's Jacobian and the
+ * scatter back to token order run in the backward's own epilogues, from the
+ * fp32 gradients, so dq, dk, dv never reach memory in cell order.
+ *   q, k, v, rnorm  as written by rt_qk_prepare from qkv, perm, tau
+ *   o, lse          as produced by rt_attention_fwd on q, k, v
+ *   d_o             gradient of o, cell order [B][H][S][Dh] bf16
+ *   dqkv            bf16 [B][S][3][H][Dh], gradient of qkv (written)
+ *   dtau_rows       fp32 [B][H][S]: per cell, the share of d tau[h]
+ *                   (sum over b and cells gives d tau)
+ * The workspace is rt_attention_bwd's. Replaces dq/dk/dv + rt_qk_prepare_bwd. */
+int rt_attention_bwd_qkv(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* o,
+                         const uint16_t* d_o, const float* lse, int32_t batch, int32_t heads,
+                         int32_t seq_len, int32_t head_dim, float scale, const rt_tile_plan* plan,
+                         const uint16_t* perm, const uint16_t* qkv, const float* tau, const float* rnorm,
+                         uint16_t* dqkv, float* dtau_rows, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
 /* Backward for callers that cannot allocate device memory (no counterpart in
  * the reference). Same arguments and results as rt_attention_bwd minus the
  * workspace: a plugin host or FFI handler without a scratch-allocation hook,

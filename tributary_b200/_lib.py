@@ -30,7 +30,7 @@ TILE = 128
 EXPORTED = (
     "rt_tile_plan_bytes", "rt_tile_plan_bind", "rt_build_tile_plan",
     "rt_attention_fwd", "rt_attention_bwd_workspace_bytes", "rt_attention_bwd",
-    "rt_attention_bwd_noalloc", "rt_column_order", "rt_rcm_order",
+    "rt_attention_bwd_noalloc", "rt_attention_bwd_qkv", "rt_column_order", "rt_rcm_order",
     "rt_qk_prepare", "rt_qk_prepare_bwd", "rt_heads_unpermute", "rt_heads_permute",
     "rt_device_status", "rt_status_string", "rt_last_error", "rt_version",
     "rt_selftest_bounded_wait", "rt_column_order_device",
@@ -96,6 +96,9 @@ def _declare(lib):
     lib.rt_attention_bwd.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, plan_p,
                                      vp, vp, vp, vp, sz, vp]
     lib.rt_attention_bwd.restype = ctypes.c_int
+    lib.rt_attention_bwd_qkv.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, plan_p,
+                                         vp, vp, vp, vp, vp, vp, vp, sz, vp]
+    lib.rt_attention_bwd_qkv.restype = ctypes.c_int
     lib.rt_attention_bwd_noalloc.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32,
                                              plan_p, vp, vp, vp, vp]
     lib.rt_attention_bwd_noalloc.restype = ctypes.c_int

@@ -316,6 +316,32 @@ int rt_attention_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, co
                               dk, dv, stats, dq_acc, aux, static_cast<cudaStream_t>(stream));
 }
 
+int rt_attention_bwd_qkv(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* o,
+                         const uint16_t* d_o, const float* lse, int32_t batch, int32_t heads,
+                         int32_t seq_len, int32_t head_dim, float scale, const rt_tile_plan* plan,
+                         const uint16_t* perm, const uint16_t* qkv, const float* tau, const float* rnorm,
+                         uint16_t* dqkv, float* dtau_rows, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  if (batch < 0 || heads < 0 || seq_len < 0 || seq_len > 65536 || batch > 65535 || heads > 65535)
+    return RT_ERR_INVALID_ARGUMENT;
+  if (head_dim != 32 && head_dim != 64) return RT_ERR_UNSUPPORTED;
+  if (!(scale > 0.f) || !(scale < INFINITY)) return RT_ERR_INVALID_ARGUMENT;
+  if (batch == 0 || heads == 0 || seq_len == 0) return RT_OK;
+  if (!plan_matches(plan, batch, seq_len)) return RT_ERR_INVALID_ARGUMENT;
+  const void* ptrs[] = {q, k, v, o, d_o, lse, perm, qkv, tau, rnorm, dqkv, dtau_rows, workspace};
+  for (const void* p : ptrs)
+    if (!p || !aligned16(p)) return RT_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < rt_attention_bwd_workspace_bytes(batch, heads, seq_len)) return RT_ERR_WORKSPACE;
+  DeviceGuard guard(q);
+  if (guard.status() != RT_OK) return guard.status();
+  const size_t padded = (size_t)((seq_len + RT_TILE - 1) / RT_TILE) * RT_TILE;
+  uint8_t* acc_base = static_cast<uint8_t*>(workspace) + bwd_stats_bytes(batch, heads, seq_len);
+  float* dq_acc = reinterpret_cast<float*>(acc_base);
+  uint16_t* aux = reinterpret_cast<uint16_t*>(acc_base + align_up(64 * sizeof(float) * (size_t)batch * heads * padded));
+  return launch_attention_bwd_qkv(q, k, v, o, d_o, lse, batch, heads, seq_len, head_dim, scale, *plan, perm, qkv,
+                                  tau, rnorm, dqkv, dtau_rows, dq_acc, aux, static_cast<cudaStream_t>(stream));
+}
+
 int rt_device_status(int32_t reset) {
   int status = 0;
   cudaError_t e = cudaDeviceSynchronize();

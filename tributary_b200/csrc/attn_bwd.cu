@@ -88,6 +88,7 @@ struct __align__(8) Barriers {
   uint64_t dq_ready;       // fused kernel: dQ partial of the tile in TMEM
   uint64_t dq_drained;     // fused kernel: the reduce warps have read the dQ partial out of TMEM
   uint64_t drain;
+  uint64_t epi_red;        // fused kernel, token outputs: every softmax warp has written its share of a row sum
 };
 
 __device__ __forceinline__ void init_barriers(Barriers& bars, int stages) {
@@ -106,6 +107,7 @@ __device__ __forceinline__ void init_barriers(Barriers& bars, int stages) {
   mbar_init(&bars.dq_ready, 1);
   mbar_init(&bars.dq_drained, 4);
   mbar_init(&bars.drain, 1);
+  mbar_init(&bars.epi_red, kSoftmaxThreads / 32);
   fence_mbar_init();
 }
 
@@ -208,6 +210,24 @@ __device__ __forceinline__ uint32_t packed_col(int ks) { return (uint32_t)((ks >
 template <int DH>
 struct EpiSlice {
   static constexpr int kCols = DH / 4 < 16 ? 16 : DH / 4;
+};
+
+// Gradients in token order for the whole sublayer step [gather + QK
+// normalisation + attention] (confluence/confluence/layers.py:63-97 and
+// 139-142), when dqkv is set: instead of dq, dk, dv in cell order, the
+// backward writes the gradient of the token-order projection qkv
+// [B][S][3][H][Dh], through the normalisation's Jacobian for q and k, and
+// per (b, h, cell) the row's share of d tau. With
+//   y = x r, r = 1 / max(|x|, 1e-6), out = s y  (s = tau_h for q, 1 for k),
+// and g the gradient of out: dx = r (s g - y yd), yd = s (y . g) while r <
+// 1e6 (else 0: the clamped norm is a constant), d tau share = y . g.
+struct TokenGrads {
+  const uint16_t* perm;  // [B][S] cell order: cell i is token perm[b][i]
+  const uint16_t* qkv;   // [B][S][3][H][Dh] the projection the forward normalised
+  const float* rnorm;    // [2][B][H][S] r of q, then of k, per cell
+  const float* tau;      // [H]
+  uint16_t* dqkv;        // [B][S][3][H][Dh]
+  float* dtau_rows;      // [B][H][S]
 };
 
 // Row statistics for the gradient kernels, padded to whole tiles and stored
@@ -727,7 +747,7 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                 const __grid_constant__ CUtensorMap tm_aux, const rt_tile_plan plan, int H, int S, float scale,
                 float scale_log2, uint16_t* __restrict__ dk, uint16_t* __restrict__ dv,
-                const __grid_constant__ CUtensorMap tm_acc) {
+                const __grid_constant__ CUtensorMap tm_acc, const TokenGrads tg) {
   using C = Cfg<DH>;
   constexpr int kST0 = 0, kDPT = 256, kDV = 384, kDK = 384 + DH;
   extern __shared__ uint8_t smem_raw[];
@@ -1021,22 +1041,76 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
     }
     if (ok && n_tiles > 0 && mbar_wait_warp(&bars.done, 0, &abort_flag)) {
       tc_fence_after();
-      uint16_t* dst_v = dv + ((size_t)bh * S + key) * DH;
-      uint16_t* dst_k = dk + ((size_t)bh * S + key) * DH;
+      if (tg.dqkv == nullptr) {
+        uint16_t* dst_v = dv + ((size_t)bh * S + key) * DH;
+        uint16_t* dst_k = dk + ((size_t)bh * S + key) * DH;
 #pragma unroll
-      for (int c = grp * EpiSlice<DH>::kCols; c < (grp + 1) * EpiSlice<DH>::kCols && c < DH; c += 16) {
-        uint32_t r[16], pko[8];
-        tmem_ld16(lane_base + kDV + c, r);
-        tmem_wait_ld();
+        for (int c = grp * EpiSlice<DH>::kCols; c < (grp + 1) * EpiSlice<DH>::kCols && c < DH; c += 16) {
+          uint32_t r[16], pko[8];
+          tmem_ld16(lane_base + kDV + c, r);
+          tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 16; e += 2) pko[e / 2] = pack_bf16x2(__uint_as_float(r[e]), __uint_as_float(r[e + 1]));
-        if (key < S) store_row_bf16(dst_v + c, pko);
-        tmem_ld16(lane_base + kDK + c, r);
-        tmem_wait_ld();
+          for (int e = 0; e < 16; e += 2) pko[e / 2] = pack_bf16x2(__uint_as_float(r[e]), __uint_as_float(r[e + 1]));
+          if (key < S) store_row_bf16(dst_v + c, pko);
+          tmem_ld16(lane_base + kDK + c, r);
+          tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 16; e += 2)
-          pko[e / 2] = pack_bf16x2(__uint_as_float(r[e]) * scale, __uint_as_float(r[e + 1]) * scale);
-        if (key < S) store_row_bf16(dst_k + c, pko);
+          for (int e = 0; e < 16; e += 2)
+            pko[e / 2] = pack_bf16x2(__uint_as_float(r[e]) * scale, __uint_as_float(r[e + 1]) * scale);
+          if (key < S) store_row_bf16(dst_k + c, pko);
+        }
+      } else {
+        // token order: dv scattered to the key's token, dk through the k
+        // normalisation's Jacobian. Each warp holds 16 columns of its 32 key
+        // rows (none for column groups past Dh); the row sum y . g adds the
+        // four groups' shares in a fixed order through shared memory (the
+        // dS^T tile, which no MMA reads any more).
+        const int c = grp * 16;
+        const bool has = c < DH;
+        const bool kin = key < S;
+        const int tok = kin ? min((int)tg.perm[(size_t)b * S + key], S - 1) : 0;  // clamps as the prepass does
+        const size_t trow = ((size_t)b * S + tok) * 3 * H * DH + (size_t)h * DH + c;
+        const float rk = kin ? tg.rnorm[((size_t)(gridDim.z + b) * H + h) * S + key] : 0.f;
+        float g[16], y[16];
+        float part = 0.f;
+        if (has) {
+          uint32_t r[16], pko[8];
+          tmem_ld16(lane_base + kDV + c, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) pko[e / 2] = pack_bf16x2(__uint_as_float(r[e]), __uint_as_float(r[e + 1]));
+          if (kin) store_row_bf16(tg.dqkv + trow + 2 * H * DH, pko);
+          tmem_ld16(lane_base + kDK + c, r);
+          tmem_wait_ld();
+          uint4 x0 = make_uint4(0u, 0u, 0u, 0u), x1 = x0;
+          if (kin) {
+            x0 = *reinterpret_cast<const uint4*>(tg.qkv + trow + H * DH);
+            x1 = *reinterpret_cast<const uint4*>(tg.qkv + trow + H * DH + 8);
+          }
+          const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            const float2 xf = unpack_bf16x2(xw[e / 2]);
+            g[e] = __uint_as_float(r[e]) * scale;
+            g[e + 1] = __uint_as_float(r[e + 1]) * scale;
+            y[e] = xf.x * rk;
+            y[e + 1] = xf.y * rk;
+            part = fmaf(y[e], g[e], part);
+            part = fmaf(y[e + 1], g[e + 1], part);
+          }
+        }
+        float* s_red = reinterpret_cast<float*>(smem + C::kDS);  // [4 groups][128 keys]
+        s_red[grp * RT_TILE + row] = part;
+        mbar_arrive_warp(&bars.epi_red);
+        if (mbar_wait_warp(&bars.epi_red, 0, &abort_flag) && has && kin) {
+          const float yg = ((s_red[row] + s_red[RT_TILE + row]) + s_red[2 * RT_TILE + row]) + s_red[3 * RT_TILE + row];
+          const float yd = rk < 1e6f ? yg : 0.f;
+          uint32_t pko[8];
+#pragma unroll
+          for (int e = 0; e < 16; e += 2)
+            pko[e / 2] = pack_bf16x2(rk * (g[e] - y[e] * yd), rk * (g[e + 1] - y[e + 1] * yd));
+          store_row_bf16(tg.dqkv + trow + H * DH, pko);
+        }
       }
     }
     tc_fence_before();
@@ -1065,10 +1139,60 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(const float* __restrict
                  pack_bf16x2(b.x * scale, b.y * scale), pack_bf16x2(b.z * scale, b.w * scale));
 }
 
+// Token-order dQ (TokenGrads): g = scale * dq_acc for the seq_len real rows,
+// through the q normalisation's Jacobian into dqkv's q slot of the cell's
+// token, and the row's d tau share. DH / 8 consecutive threads hold one row,
+// 8 elements each; the row sum is a shuffle reduction among them.
+template <int DH>
+__global__ void __launch_bounds__(256) dq_qkv_kernel(const float* __restrict__ dq_acc, long long rows, int H, int S,
+                                                     int Sp, float scale, const TokenGrads tg) {
+  constexpr int kLanes = DH / 8;
+  const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long row = gid / kLanes;
+  const bool valid = row < rows;  // every lane stays for the shuffles below
+  const int c = (int)(gid % kLanes) * 8;
+  const long long bh = valid ? row / S : 0;
+  const int i = valid ? (int)(row % S) : 0;
+  const int b = (int)(bh / H), h = (int)(bh % H);
+  float g[8], y[8];
+  float part = 0.f, rq = 0.f, t = 0.f;
+  size_t trow = 0;
+  if (valid) {
+    const float4* src = reinterpret_cast<const float4*>(dq_acc + ((size_t)bh * Sp + i) * DH + c);
+    const float4 a0 = src[0], a1 = src[1];
+    g[0] = a0.x * scale; g[1] = a0.y * scale; g[2] = a0.z * scale; g[3] = a0.w * scale;
+    g[4] = a1.x * scale; g[5] = a1.y * scale; g[6] = a1.z * scale; g[7] = a1.w * scale;
+    const int tok = min((int)tg.perm[(size_t)b * S + i], S - 1);  // clamps as the prepass does
+    trow = ((size_t)b * S + tok) * 3 * H * DH + (size_t)h * DH + c;
+    rq = tg.rnorm[((size_t)b * H + h) * S + i];
+    t = tg.tau[h];
+    const uint4 x = *reinterpret_cast<const uint4*>(tg.qkv + trow);
+    const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      const float2 xf = unpack_bf16x2(xw[e / 2]);
+      y[e] = xf.x * rq;
+      y[e + 1] = xf.y * rq;
+      part = fmaf(y[e], g[e], part);
+      part = fmaf(y[e + 1], g[e + 1], part);
+    }
+  }
+#pragma unroll
+  for (int off = 1; off < kLanes; off <<= 1) part += __shfl_xor_sync(0xFFFFFFFFu, part, off);
+  if (!valid) return;
+  const float yd = rq < 1e6f ? t * part : 0.f;
+  uint32_t pk[4];
+#pragma unroll
+  for (int e = 0; e < 8; e += 2) pk[e / 2] = pack_bf16x2(rq * (t * g[e] - y[e] * yd), rq * (t * g[e + 1] - y[e + 1] * yd));
+  *reinterpret_cast<uint4*>(tg.dqkv + trow) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  if (c == 0) tg.dtau_rows[((size_t)b * H + h) * S + i] = part;
+}
+
 template <int DH>
 int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* o, const uint16_t* d_o,
            const float* lse, int B, int H, int S, float scale, const rt_tile_plan& plan, uint16_t* dq,
-           uint16_t* dk, uint16_t* dv, float* stats, float* dq_acc, uint16_t* aux, cudaStream_t stream) {
+           uint16_t* dk, uint16_t* dv, float* stats, float* dq_acc, uint16_t* aux, const TokenGrads& tg,
+           cudaStream_t stream) {
   using C = Cfg<DH>;
   CUtensorMap tq, tk, tv, tdo;
   if (make_qkv_tensor_map(&tq, q, B * H, S, DH) != RT_OK || make_qkv_tensor_map(&tk, k, B * H, S, DH) != RT_OK ||
@@ -1103,10 +1227,14 @@ int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16
     if (make_acc_tensor_map(&tacc, dq_acc, rows_padded, DH) != RT_OK) return RT_ERR_CUDA;
     if (make_aux_tensor_map(&taux, aux, rows_padded) != RT_OK) return RT_ERR_CUDA;
     dkdvq_kernel<DH><<<grid, kThreadsFused, C::kDynSmemFused, stream>>>(tq, tk, tv, tdo, taux, plan, H, S, scale,
-                                                                   scale_log2, dk, dv, tacc);
+                                                                   scale_log2, dk, dv, tacc, tg);
     if (int st = check_launch("dkdvq_kernel launch")) return st;
     const long long rows = (long long)B * H * S;
     const long long cthreads = rows * (DH / 8);
+    if (tg.dqkv != nullptr) {
+      dq_qkv_kernel<DH><<<(unsigned)((cthreads + 255) / 256), 256, 0, stream>>>(dq_acc, rows, H, S, Sp, scale, tg);
+      return check_launch("dq_qkv_kernel launch");
+    }
     dq_convert_kernel<DH><<<(unsigned)((cthreads + 255) / 256), 256, 0, stream>>>(dq_acc, dq, rows, S, Sp, scale);
     return check_launch("dq_convert_kernel launch");
   }
@@ -1124,10 +1252,26 @@ int launch_attention_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v
                          const uint16_t* d_o, const float* lse, int B, int H, int S, int Dh, float scale,
                          const rt_tile_plan& plan, uint16_t* dq, uint16_t* dk, uint16_t* dv, float* stats,
                          float* dq_acc, uint16_t* aux, cudaStream_t stream) {
+  const bwd::TokenGrads none{};
   if (Dh == 64)
-    return bwd::launch<64>(q, k, v, o, d_o, lse, B, H, S, scale, plan, dq, dk, dv, stats, dq_acc, aux, stream);
+    return bwd::launch<64>(q, k, v, o, d_o, lse, B, H, S, scale, plan, dq, dk, dv, stats, dq_acc, aux, none, stream);
   if (Dh == 32)
-    return bwd::launch<32>(q, k, v, o, d_o, lse, B, H, S, scale, plan, dq, dk, dv, stats, dq_acc, aux, stream);
+    return bwd::launch<32>(q, k, v, o, d_o, lse, B, H, S, scale, plan, dq, dk, dv, stats, dq_acc, aux, none, stream);
+  return RT_ERR_UNSUPPORTED;
+}
+
+int launch_attention_bwd_qkv(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* o,
+                             const uint16_t* d_o, const float* lse, int B, int H, int S, int Dh, float scale,
+                             const rt_tile_plan& plan, const uint16_t* perm, const uint16_t* qkv, const float* tau,
+                             const float* rnorm, uint16_t* dqkv, float* dtau_rows, float* dq_acc, uint16_t* aux,
+                             cudaStream_t stream) {
+  const bwd::TokenGrads tg{perm, qkv, rnorm, tau, dqkv, dtau_rows};
+  if (Dh == 64)
+    return bwd::launch<64>(q, k, v, o, d_o, lse, B, H, S, scale, plan, nullptr, nullptr, nullptr, nullptr, dq_acc,
+                           aux, tg, stream);
+  if (Dh == 32)
+    return bwd::launch<32>(q, k, v, o, d_o, lse, B, H, S, scale, plan, nullptr, nullptr, nullptr, nullptr, dq_acc,
+                           aux, tg, stream);
   return RT_ERR_UNSUPPORTED;
 }
 

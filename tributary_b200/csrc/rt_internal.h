@@ -29,6 +29,14 @@ int launch_attention_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v
                          float scale, const rt_tile_plan& plan, uint16_t* dq, uint16_t* dk,
                          uint16_t* dv, float* stats, float* dq_acc, uint16_t* aux, cudaStream_t stream);
 
+// The fused backward with token-order outputs for the sublayer step [gather +
+// QK normalisation + attention]: dqkv [B][S][3][H][Dh] and d tau row shares.
+int launch_attention_bwd_qkv(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* o,
+                             const uint16_t* d_o, const float* lse, int B, int H, int S, int Dh, float scale,
+                             const rt_tile_plan& plan, const uint16_t* perm, const uint16_t* qkv, const float* tau,
+                             const float* rnorm, uint16_t* dqkv, float* dtau_rows, float* dq_acc, uint16_t* aux,
+                             cudaStream_t stream);
+
 // TMA descriptor for a [rows_total][Dh] bf16 matrix viewed as (Dh, S, B*H),
 // box (Dh, 128, 1), 128B swizzle for Dh = 64, 64B swizzle for Dh = 32.
 int make_qkv_tensor_map(CUtensorMap* map, const void* base, int BH, int S, int Dh);

@@ -16,6 +16,8 @@
 //                order <-> [B,S,H*Dh] in token order (each other's backward)
 // One warp per token; a warp moves each head's Dh-element row as one
 // contiguous, coalesced access. Norms and products are accumulated in fp32.
+// Order entries past the end clamp to S - 1, as in the prepass, so no order
+// can move an access out of bounds.
 #include "rt_device.cuh"
 #include "rt_internal.h"
 
@@ -79,7 +81,7 @@ __global__ void __launch_bounds__(32 * kWarps) qk_prepare_kernel(const uint16_t*
   if (t >= (long long)B * S) return;
   const int b = (int)(t / S), i = (int)(t % S);
   const int D = H * DH;
-  const uint16_t* row = qkv + ((size_t)b * S + perm[t]) * 3 * D;
+  const uint16_t* row = qkv + ((size_t)b * S + min((int)perm[t], S - 1)) * 3 * D;
   for (int h = 0; h < H; ++h) {
     const size_t o = (((size_t)b * H + h) * S + i) * DH;
     Lane<DH> x;
@@ -128,7 +130,7 @@ __global__ void __launch_bounds__(32 * kWarps) qk_prepare_bwd_kernel(
   if (t >= (long long)B * S) return;
   const int b = (int)(t / S), i = (int)(t % S);
   const int D = H * DH;
-  const size_t r0 = ((size_t)b * S + perm[t]) * 3 * D;
+  const size_t r0 = ((size_t)b * S + min((int)perm[t], S - 1)) * 3 * D;
   for (int h = 0; h < H; ++h) {
     const size_t o = (((size_t)b * H + h) * S + i) * DH;
     const float rq = rnorm[((size_t)b * H + h) * S + i];
@@ -149,7 +151,7 @@ __global__ void __launch_bounds__(32 * kWarps) heads_reorder_kernel(const uint16
   const long long t = (long long)blockIdx.x * kWarps + (threadIdx.x >> 5);
   if (t >= (long long)B * S) return;
   const int b = (int)(t / S), i = (int)(t % S);
-  const size_t tok = ((size_t)b * S + perm[t]) * H * DH;
+  const size_t tok = ((size_t)b * S + min((int)perm[t], S - 1)) * H * DH;
   for (int h = 0; h < H; ++h) {
     const size_t o = (((size_t)b * H + h) * S + i) * DH;
     if (kToTokens)

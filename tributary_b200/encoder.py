@@ -14,7 +14,9 @@ sublayer, attention runs in the kind's cell order (layers.py:139-167): the QKV
 projection is applied in token order (a per-token linear map commutes with the
 gather), then one kernel gathers, splits heads and L2-normalises q and k with
 tau (rt_qk_prepare), the attention kernels run under the kind's tile plan, and
-one kernel returns the output to token order (rt_heads_unpermute).
+one kernel returns the output to token order (rt_heads_unpermute). In the
+backward, one call (rt_attention_bwd_qkv) runs the attention backward with the
+normalisation's Jacobian and the scatter back to token order in its epilogues.
 
 Matmuls run under bf16 autocast with fp32 parameters and an fp32 residual
 stream; norms, QK normalisation and softmax statistics are computed in fp32
@@ -71,7 +73,8 @@ class ZeroCenteredRMSNorm(nn.Module):
 class KernelOps:
     """The encoder's token preparation, attention and fused layer kernels on
     the library: ``order`` is the [B,S] int16 cell order, ``ctx`` the
-    TilePlan; rms_norm, gate_residual and swiglu are one kernel each way."""
+    TilePlan; rms_norm, gate_residual and swiglu are one kernel each way, and
+    qk_attention is token preparation + attention with one fused backward."""
 
     @staticmethod
     def rms_norm(x, gamma, eps):
@@ -103,6 +106,11 @@ class KernelOps:
         return rt_attention(q, k, v, ctx, scale)
 
     @staticmethod
+    def qk_attention(qkv, order, tau, heads, head_dim, ctx, scale):
+        from .tokens import qk_attention
+        return qk_attention(qkv, order, tau, heads, head_dim, ctx, scale)
+
+    @staticmethod
     def heads_unpermute(o, order):
         from .tokens import heads_unpermute
         return heads_unpermute(o, order)
@@ -132,8 +140,13 @@ class GatedAttention(nn.Module):
         cfg = self.cfg
         h, dh = cfg.n_heads, cfg.d_head
         x_norm = self.norm(x, ops)
-        q, k, v = ops.qk_prepare(self.qkv(x_norm), order, self.tau, h, dh)
-        o = ops.heads_unpermute(ops.attention(q, k, v, mask_ctx, 1.0 / math.sqrt(dh)), order)
+        scale = 1.0 / math.sqrt(dh)
+        if hasattr(ops, "qk_attention"):  # one backward for gather, QK norm and attention
+            o = ops.qk_attention(self.qkv(x_norm), order, self.tau, h, dh, mask_ctx, scale)
+        else:
+            q, k, v = ops.qk_prepare(self.qkv(x_norm), order, self.tau, h, dh)
+            o = ops.attention(q, k, v, mask_ctx, scale)
+        o = ops.heads_unpermute(o, order)
         if not torch.is_autocast_enabled(o.device.type):  # autocast feeds W_O bf16 as it is
             o = o.to(x.dtype)
         return ops.gate_residual(x, self.wo(o), self.w_gate(x_norm), self.output_scale)
