@@ -88,7 +88,7 @@ struct __align__(8) Barriers {
   uint64_t dq_ready;       // fused kernel: dQ partial of the tile in TMEM
   uint64_t dq_drained;     // fused kernel: the reduce warps have read the dQ partial out of TMEM
   uint64_t drain;
-  uint64_t epi_red;        // fused kernel, token outputs: every softmax warp has written its share of a row sum
+  uint64_t epi_red;        // fused kernel, token outputs: every softmax warp has written its share of the row sums
 };
 
 __device__ __forceinline__ void init_barriers(Barriers& bars, int stages) {
@@ -741,7 +741,7 @@ __device__ __forceinline__ void softmax_phase_b_aux(uint32_t taddr, const uint32
   }
 }
 
-template <int DH>
+template <int DH, bool kTok>
 __global__ void __launch_bounds__(kThreadsFused, 1)
     dkdvq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
@@ -949,6 +949,16 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     uint8_t* slot = smem + C::kStg + (warp - 2 - kSoftmaxThreads / 32) * C::kStgSlot;
     int rb = 0;  // ring position of the next box
+    // Token-order outputs (TokenGrads): the softmax warps' epilogue reads each
+    // key row's order entry and k inverse norm; they start on their way into
+    // L2 now, while this warp has nothing to drain yet.
+    if (kTok) {
+      const int key = kt * RT_TILE + quad * 32 + lane;
+      if (key < S) {
+        prefetch_l2(tg.perm + (size_t)b * S + key);
+        prefetch_l2(tg.rnorm + ((size_t)(gridDim.z + b) * H + h) * S + key);
+      }
+    }
     for (int t = 0; t < n_tiles; ++t) {
       if (!mbar_wait_warp(&bars.dq_ready, t & 1, &abort_flag)) break;
       tc_fence_after();
@@ -1041,7 +1051,7 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
     }
     if (ok && n_tiles > 0 && mbar_wait_warp(&bars.done, 0, &abort_flag)) {
       tc_fence_after();
-      if (tg.dqkv == nullptr) {
+      if (!kTok) {
         uint16_t* dst_v = dv + ((size_t)bh * S + key) * DH;
         uint16_t* dst_k = dk + ((size_t)bh * S + key) * DH;
 #pragma unroll
@@ -1060,56 +1070,64 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
           if (key < S) store_row_bf16(dst_k + c, pko);
         }
       } else {
-        // token order: dv scattered to the key's token, dk through the k
-        // normalisation's Jacobian. Each warp holds 16 columns of its 32 key
-        // rows (none for column groups past Dh); the row sum y . g adds the
-        // four groups' shares in a fixed order through shared memory (the
-        // dS^T tile, which no MMA reads any more).
+        // token order (TokenGrads): dv scattered to the key's token, dk
+        // through the k normalisation's Jacobian. Each warp holds 16 columns
+        // of its 32 key rows (none for column groups past Dh). y = x r is
+        // k_hat, the row of the resident K tile (the bf16 value the forward
+        // used), so y . g needs no global load: each warp forms its share
+        // from TMEM and shared memory, and the four shares of a row are added
+        // in a fixed order through shared memory (the dS^T tile, which no MMA
+        // reads any more) behind a bounded barrier.
         const int c = grp * 16;
         const bool has = c < DH;
         const bool kin = key < S;
         const int tok = kin ? min((int)tg.perm[(size_t)b * S + key], S - 1) : 0;  // clamps as the prepass does
-        const size_t trow = ((size_t)b * S + tok) * 3 * H * DH + (size_t)h * DH + c;
         const float rk = kin ? tg.rnorm[((size_t)(gridDim.z + b) * H + h) * S + key] : 0.f;
-        float g[16], y[16];
+        uint32_t g[16], kw[8];
         float part = 0.f;
         if (has) {
-          uint32_t r[16], pko[8];
-          tmem_ld16(lane_base + kDV + c, r);
+          uint32_t pk[8];
+          tmem_ld16(lane_base + kDV + c, g);
           tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 16; e += 2) pko[e / 2] = pack_bf16x2(__uint_as_float(r[e]), __uint_as_float(r[e + 1]));
-          if (kin) store_row_bf16(tg.dqkv + trow + 2 * H * DH, pko);
-          tmem_ld16(lane_base + kDK + c, r);
-          tmem_wait_ld();
-          uint4 x0 = make_uint4(0u, 0u, 0u, 0u), x1 = x0;
-          if (kin) {
-            x0 = *reinterpret_cast<const uint4*>(tg.qkv + trow + H * DH);
-            x1 = *reinterpret_cast<const uint4*>(tg.qkv + trow + H * DH + 8);
+          for (int e = 0; e < 16; e += 2) pk[e / 2] = pack_bf16x2(__uint_as_float(g[e]), __uint_as_float(g[e + 1]));
+          const size_t trow = ((size_t)b * S + tok) * 3 * H * DH + (size_t)h * DH + c;
+          if (kin) store_row_bf16(tg.dqkv + trow + 2 * H * DH, pk);
+          tmem_ld16(lane_base + kDK + c, g);
+          // 16-byte chunks c / 8 and c / 8 + 1 of the K tile's row: 128-byte
+          // swizzle for DH = 64 (chunk j of row r at j ^ (r % 8)), 64-byte for
+          // DH = 32 (at j ^ ((r / 2) % 4))
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int ch = c / 8 + j;
+            const int off = DH == 64 ? row * 128 + ((ch ^ (row & 7)) << 4) : row * 64 + ((ch ^ ((row >> 1) & 3)) << 4);
+            const uint4 v = *reinterpret_cast<const uint4*>(smem + C::kA0 + off);
+            kw[4 * j] = v.x;
+            kw[4 * j + 1] = v.y;
+            kw[4 * j + 2] = v.z;
+            kw[4 * j + 3] = v.w;
           }
-          const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+          tmem_wait_ld();
 #pragma unroll
           for (int e = 0; e < 16; e += 2) {
-            const float2 xf = unpack_bf16x2(xw[e / 2]);
-            g[e] = __uint_as_float(r[e]) * scale;
-            g[e + 1] = __uint_as_float(r[e + 1]) * scale;
-            y[e] = xf.x * rk;
-            y[e + 1] = xf.y * rk;
-            part = fmaf(y[e], g[e], part);
-            part = fmaf(y[e + 1], g[e + 1], part);
+            const float2 y = unpack_bf16x2(kw[e / 2]);
+            part = fmaf(y.x, __uint_as_float(g[e]) * scale, part);
+            part = fmaf(y.y, __uint_as_float(g[e + 1]) * scale, part);
           }
         }
-        float* s_red = reinterpret_cast<float*>(smem + C::kDS);  // [4 groups][128 keys]
+        float* s_red = reinterpret_cast<float*>(smem + C::kDS);  // [4 column groups][128 keys]
         s_red[grp * RT_TILE + row] = part;
         mbar_arrive_warp(&bars.epi_red);
         if (mbar_wait_warp(&bars.epi_red, 0, &abort_flag) && has && kin) {
           const float yg = ((s_red[row] + s_red[RT_TILE + row]) + s_red[2 * RT_TILE + row]) + s_red[3 * RT_TILE + row];
           const float yd = rk < 1e6f ? yg : 0.f;
-          uint32_t pko[8];
 #pragma unroll
-          for (int e = 0; e < 16; e += 2)
-            pko[e / 2] = pack_bf16x2(rk * (g[e] - y[e] * yd), rk * (g[e + 1] - y[e + 1] * yd));
-          store_row_bf16(tg.dqkv + trow + H * DH, pko);
+          for (int e = 0; e < 16; e += 2) {
+            const float2 y = unpack_bf16x2(kw[e / 2]);
+            kw[e / 2] = pack_bf16x2(rk * (__uint_as_float(g[e]) * scale - y.x * yd),
+                                    rk * (__uint_as_float(g[e + 1]) * scale - y.y * yd));
+          }
+          store_row_bf16(tg.dqkv + ((size_t)b * S + tok) * 3 * H * DH + (size_t)(H + h) * DH + c, kw);
         }
       }
     }
@@ -1206,8 +1224,10 @@ int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16
     if (e != cudaSuccess) return cuda_failure(e, "cudaFuncSetAttribute(dq_kernel)");
     e = cudaFuncSetAttribute(dkdv_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kDynSmem);
     if (e != cudaSuccess) return cuda_failure(e, "cudaFuncSetAttribute(dkdv_kernel)");
-    e = cudaFuncSetAttribute(dkdvq_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kDynSmemFused);
+    e = cudaFuncSetAttribute(dkdvq_kernel<DH, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kDynSmemFused);
     if (e != cudaSuccess) return cuda_failure(e, "cudaFuncSetAttribute(dkdvq_kernel)");
+    e = cudaFuncSetAttribute(dkdvq_kernel<DH, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kDynSmemFused);
+    if (e != cudaSuccess) return cuda_failure(e, "cudaFuncSetAttribute(dkdvq_kernel, token outputs)");
     configured[dev] = true;
   }
   const int Sp = plan.tiles * RT_TILE;
@@ -1226,8 +1246,12 @@ int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16
     CUtensorMap tacc, taux;
     if (make_acc_tensor_map(&tacc, dq_acc, rows_padded, DH) != RT_OK) return RT_ERR_CUDA;
     if (make_aux_tensor_map(&taux, aux, rows_padded) != RT_OK) return RT_ERR_CUDA;
-    dkdvq_kernel<DH><<<grid, kThreadsFused, C::kDynSmemFused, stream>>>(tq, tk, tv, tdo, taux, plan, H, S, scale,
-                                                                   scale_log2, dk, dv, tacc, tg);
+    if (tg.dqkv != nullptr)
+      dkdvq_kernel<DH, true><<<grid, kThreadsFused, C::kDynSmemFused, stream>>>(tq, tk, tv, tdo, taux, plan, H, S,
+                                                                             scale, scale_log2, dk, dv, tacc, tg);
+    else
+      dkdvq_kernel<DH, false><<<grid, kThreadsFused, C::kDynSmemFused, stream>>>(tq, tk, tv, tdo, taux, plan, H, S,
+                                                                              scale, scale_log2, dk, dv, tacc, tg);
     if (int st = check_launch("dkdvq_kernel launch")) return st;
     const long long rows = (long long)B * H * S;
     const long long cthreads = rows * (DH / 8);

@@ -125,6 +125,11 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, v
 // ---------------------------------------------------------------------------
 // TMA (tiled, no multicast)
 // ---------------------------------------------------------------------------
+// Start moving the 128-byte line holding p into L2 (no register result).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p) : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
