@@ -786,9 +786,12 @@ class TrainRun:
     """The config-d training step on this rank's GPU: its own B=32 shard of
     cells, a replica with the same initial weights on every rank, and a
     TrainStep whose gradient buckets are all-reduced over NCCL (reduce=True)
-    or kept local (reduce=False, the single-GPU step on the same device)."""
+    or kept local (reduce=False, the single-GPU step on the same device).
+    graph=True (steps without an all-reduce) records the whole step as one
+    CUDA graph and replays it: the cells are static tensors that a new batch
+    is copied into."""
 
-    def __init__(self, cfg, rank, dev, reduce=True):
+    def __init__(self, cfg, rank, dev, reduce=True, graph=False):
         import torch
         from tributary_b200.encoder import RTEncoder
         from tributary_b200.train import TrainStep
@@ -802,10 +805,14 @@ class TrainRun:
         self.cat = torch.from_numpy(cells["cat_table"]).to(dev)
         torch.manual_seed(1234)  # identical initial weights on every rank
         self.model = RTEncoder(encoder_config(cfg)).to(dev)
-        self.step = TrainStep(self.model, reduce=reduce)
+        self.step = TrainStep(self.model, reduce=reduce, capturable=graph)
+        if graph:
+            self.step.capture(self.d, self.col, self.cat, TRAIN_KINDS)
 
     def __call__(self):
         from tributary_b200.train import build_masks
+        if self.step.graph is not None:
+            return self.step.replay()
         return self.step(self.d, build_masks(self.d, TRAIN_KINDS), self.col, self.cat)
 
     def timed(self, steps, world, finish_events=False):
@@ -867,6 +874,14 @@ def measure_train(cfg, steps, warmup, world, rank, local):
     solo_ms, _, _ = solo.timed(steps, world)
     del solo
     torch.cuda.empty_cache()
+    graph_ms = None
+    if world == 1:  # the same step recorded once as a CUDA graph and replayed
+        gr = TrainRun(cfg, rank, dev, reduce=False, graph=True)
+        for _ in range(warmup):
+            gr()
+        graph_ms, _, _ = gr.timed(steps, world)
+        del gr
+        torch.cuda.empty_cache()
     status = device_status(reset=True)
     if status != 0 or not math.isfinite(loss_val):
         raise RuntimeError(f"training step: device status {status}, loss {loss_val}")
@@ -877,6 +892,7 @@ def measure_train(cfg, steps, warmup, world, rank, local):
                                   f"in {n_buckets} buckets, launched from post-accumulate hooks during backward",
                           "exposed_ms_per_step": exposed_ms},
             "ms_per_step_without_allreduce": solo_ms,
+            "ms_per_step_cuda_graph": graph_ms,
             "efficiency_vs_1gpu": solo_ms / dp_ms,
             "replica_param_checksum_rel_spread": spread, "final_loss": loss_val}
 
@@ -887,7 +903,8 @@ def run_train_arm(args, cfg):
     from tributary_b200.train import build_masks
     world, rank, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
-    run = TrainRun(cfg, rank, dev)
+    graph = world == 1 and not args.no_graph  # one GPU: the step replays from a CUDA graph
+    run = TrainRun(cfg, rank, dev, reduce=not graph, graph=graph)
     for _ in range(args.warmup):
         run()
     barrier(world)
@@ -896,7 +913,7 @@ def run_train_arm(args, cfg):
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
-    step_ms, exposed_ms, loss = run.timed(args.steps, world, finish_events=True)
+    step_ms, exposed_ms, loss = run.timed(args.steps, world, finish_events=not graph)
     clocks = sampler.stop()
     # end to end: every step copies its cell arrays from pinned host memory and reads the loss back
     h2d = sum(v.numel() * v.element_size() for v in run.host.values())
@@ -929,8 +946,10 @@ def run_train_arm(args, cfg):
                        "Dh": cfg["Dh"], "params": n_params, "masks_per_layer": [KIND_NAMES[k] for k in TRAIN_KINDS],
                        "optimizer": "muon (2-D weights) + adamw, global-norm clip 1.0",
                        "l2": "working set (activations of 48 sublayers) far above L2",
-                       "parallelism": f"dp{world}: NCCL all-reduce (average) of fp32 gradients in "
-                                      f"{len(run.step.buckets.buffers)} buckets, overlapped with backward"},
+                       "parallelism": (f"dp{world}: NCCL all-reduce (average) of fp32 gradients in "
+                                       f"{len(run.step.buckets.buffers)} buckets, overlapped with backward")
+                                      if world > 1 else "dp1: one GPU, no collective",
+                       "cuda_graph": graph},
             "allreduce_exposed_ms_per_step": exposed_ms,
             "roofline": {"bound": "tensor", "kernel": "whole training step (matmuls + attention)",
                          "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
@@ -1077,6 +1096,8 @@ def main():
                     help="attention workloads: skip the data-parallel training-step record")
     ap.add_argument("--no-sweep", action="store_true",
                     help="attention workloads: skip the B=32 S=1024 record and the length x density sweep")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="--config d on one GPU: run the step eagerly instead of replaying a CUDA graph")
     ap.add_argument("--train-steps", type=int, default=10,
                     help="timed steps of the training-step record")
     ap.add_argument("--batch", type=int, default=None,

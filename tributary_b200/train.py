@@ -241,7 +241,7 @@ class TrainStep:
     def __init__(self, model, group=None, muon_lr: float = 0.02, adamw_lr: float = 3e-4,
                  weight_decay: float = 0.1, max_grad_norm: float = 1.0, bucket_bytes: int = 32 << 20,
                  autocast: bool = True, reduce: bool = True, heartbeat: Heartbeat | None = None,
-                 allreduce_timeout_s: float | None = None):
+                 allreduce_timeout_s: float | None = None, capturable: bool = False):
         self.model = model
         self.heartbeat = heartbeat
         self.allreduce_timeout_s = allreduce_timeout_s
@@ -254,15 +254,59 @@ class TrainStep:
         rest = [p for p in model.parameters() if p.requires_grad and p.ndim != 2]
         dev = next(model.parameters()).device
         self.muon = Muon(mats, lr=muon_lr)
+        # capturable: the optimizer's step counters stay on the device, so the
+        # whole step can be replayed from a CUDA graph (capture())
         self.adamw = torch.optim.AdamW(rest, lr=adamw_lr, betas=(0.9, 0.95), eps=1e-8,
-                                       weight_decay=weight_decay, fused=dev.type == "cuda")
+                                       weight_decay=weight_decay, fused=dev.type == "cuda",
+                                       capturable=capturable and dev.type == "cuda")
+        self.capturable = capturable
         self.max_grad_norm = max_grad_norm
         self.autocast = autocast and dev.type == "cuda"
+        self.graph = None
+        self.graph_loss = None
 
     def __call__(self, cells, masks, col_table, cat_table) -> torch.Tensor:
         if self.heartbeat is not None:  # every rank is here before any collective of this step
             self.heartbeat.step(self.steps)
         self.steps += 1
+        return self._step(cells, masks, col_table, cat_table)
+
+    def capture(self, cells, col_table, cat_table, kinds, warmup: int = 3) -> None:
+        """Record one whole step -- the tile plans of ``kinds`` built from the
+        device tensors of ``cells``, forward, loss, backward, clipping and both
+        optimizer updates -- as a CUDA graph, after ``warmup`` eager steps on a
+        side stream (which also create the optimizer state). Every replay()
+        then reads ``cells`` in place: copy each new batch into those tensors
+        first. Needs capturable=True; steps without a cross-rank collective
+        only (the gradient all-reduce stays eager)."""
+        if not self.capturable:
+            raise ValueError("TrainStep(capturable=True) is needed for capture()")
+        if self.buckets.world > 1:
+            raise ValueError("capture() covers steps without a gradient all-reduce")
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self._step(cells, build_masks(cells, kinds), col_table, cat_table)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            loss = self._step(cells, build_masks(cells, kinds), col_table, cat_table)
+        self.graph, self.graph_loss = graph, loss
+
+    def replay(self) -> torch.Tensor:
+        """One captured step on the current contents of the captured cells;
+        returns the (static) loss tensor, valid until the next replay."""
+        if self.graph is None:
+            raise RuntimeError("capture() first")
+        if self.heartbeat is not None:
+            self.heartbeat.step(self.steps)
+        self.steps += 1
+        self.graph.replay()
+        return self.graph_loss
+
+    def _step(self, cells, masks, col_table, cat_table) -> torch.Tensor:
         self.buckets.zero()
         with torch.autocast("cuda", dtype=torch.bfloat16, enabled=self.autocast):
             out = self.model(cells, masks, col_table, cat_table)
