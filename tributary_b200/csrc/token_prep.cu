@@ -70,31 +70,62 @@ __device__ __forceinline__ void copy_row(uint16_t* dst, const uint16_t* src, int
     dst[lane] = src[lane];
 }
 
+// qk_prepare: one warp per token. The token's 3 H rows (q heads, k heads, v
+// heads; Dh bf16 each) are read as 16-byte chunks, DH / 8 lanes per row and
+// 32 / (DH / 8) rows per warp instruction, with up to kBatch instructions'
+// loads in flight before any row is reduced: the kernel streams from HBM
+// instead of waiting on one small load per head.
 template <int DH>
 __global__ void __launch_bounds__(32 * kWarps) qk_prepare_kernel(const uint16_t* __restrict__ qkv,
                                                                  const uint16_t* __restrict__ perm,
                                                                  const float* __restrict__ tau, int B, int H, int S,
                                                                  uint16_t* __restrict__ q, uint16_t* __restrict__ k,
                                                                  uint16_t* __restrict__ v, float* __restrict__ rnorm) {
+  constexpr int kL = DH / 8;      // lanes per row
+  constexpr int kRows = 32 / kL;  // rows per warp instruction
+  constexpr int kBatch = 6;       // instructions whose loads are issued together
   const int lane = threadIdx.x & 31;
   const long long t = (long long)blockIdx.x * kWarps + (threadIdx.x >> 5);
-  if (t >= (long long)B * S) return;
+  if (t >= (long long)B * S) return;  // warp-uniform
   const int b = (int)(t / S), i = (int)(t % S);
-  const int D = H * DH;
-  const uint16_t* row = qkv + ((size_t)b * S + min((int)perm[t], S - 1)) * 3 * D;
-  for (int h = 0; h < H; ++h) {
-    const size_t o = (((size_t)b * H + h) * S + i) * DH;
-    Lane<DH> x;
-    x.load(row + h * DH, lane);
-    const float rq = 1.f / fmaxf(sqrtf(warp_sum(x.dot(x))), 1e-6f);
-    x.store(q + o, lane, rq * tau[h]);
-    x.load(row + D + h * DH, lane);
-    const float rk = 1.f / fmaxf(sqrtf(warp_sum(x.dot(x))), 1e-6f);
-    x.store(k + o, lane, rk);
-    copy_row<DH>(v + o, row + 2 * D + h * DH, lane);
-    if (lane == 0) {
-      rnorm[((size_t)b * H + h) * S + i] = rq;
-      rnorm[(((size_t)B + b) * H + h) * S + i] = rk;
+  const int sub = lane % kL, rsel = lane / kL;
+  const uint16_t* row = qkv + ((size_t)b * S + min((int)perm[t], S - 1)) * 3 * H * DH;
+  const int nrows = 3 * H;
+  for (int r0 = 0; r0 < nrows; r0 += kRows * kBatch) {
+    uint4 x[kBatch];
+#pragma unroll
+    for (int p = 0; p < kBatch; ++p) {
+      const int r = r0 + p * kRows + rsel;
+      x[p] = r < nrows ? *reinterpret_cast<const uint4*>(row + (size_t)r * DH + sub * 8) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int p = 0; p < kBatch; ++p) {
+      const int r = r0 + p * kRows + rsel;  // the kL lanes of a row share r
+      const uint32_t w[4] = {x[p].x, x[p].y, x[p].z, x[p].w};
+      float f[8];
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 u = unpack_bf16x2(w[e]);
+        f[2 * e] = u.x;
+        f[2 * e + 1] = u.y;
+        ss = fmaf(u.x, u.x, fmaf(u.y, u.y, ss));
+      }
+#pragma unroll
+      for (int off = 1; off < kL; off <<= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);
+      if (r >= nrows) continue;
+      const int part = r / H, h = r % H;  // 0: q, 1: k, 2: v
+      const size_t o = (((size_t)b * H + h) * S + i) * DH + sub * 8;
+      if (part == 2) {
+        *reinterpret_cast<uint4*>(v + o) = x[p];
+        continue;
+      }
+      const float rn = 1.f / fmaxf(sqrtf(ss), 1e-6f);
+      const float sc = part == 0 ? rn * tau[h] : rn;
+      *reinterpret_cast<uint4*>((part == 0 ? q : k) + o) =
+          make_uint4(pack_bf16x2(f[0] * sc, f[1] * sc), pack_bf16x2(f[2] * sc, f[3] * sc),
+                     pack_bf16x2(f[4] * sc, f[5] * sc), pack_bf16x2(f[6] * sc, f[7] * sc));
+      if (sub == 0) rnorm[(((size_t)part * B + b) * H + h) * S + i] = rn;
     }
   }
 }
