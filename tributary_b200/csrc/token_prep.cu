@@ -174,21 +174,36 @@ __global__ void __launch_bounds__(32 * kWarps) qk_prepare_bwd_kernel(
 }
 
 // kToTokens: [B,H,S,Dh] permuted -> [B,S,H*Dh] token order; else the reverse.
+// One warp per token, its H rows moved as 16-byte chunks (DH / 8 lanes per
+// row, 32 / (DH / 8) rows per warp instruction), up to kBatch instructions'
+// loads in flight before the stores.
 template <int DH, bool kToTokens>
 __global__ void __launch_bounds__(32 * kWarps) heads_reorder_kernel(const uint16_t* __restrict__ src,
                                                                     const uint16_t* __restrict__ perm, int B, int H,
                                                                     int S, uint16_t* __restrict__ dst) {
+  constexpr int kL = DH / 8;
+  constexpr int kRows = 32 / kL;
+  constexpr int kBatch = 4;
   const int lane = threadIdx.x & 31;
   const long long t = (long long)blockIdx.x * kWarps + (threadIdx.x >> 5);
   if (t >= (long long)B * S) return;
   const int b = (int)(t / S), i = (int)(t % S);
+  const int sub = lane % kL, rsel = lane / kL;
   const size_t tok = ((size_t)b * S + min((int)perm[t], S - 1)) * H * DH;
-  for (int h = 0; h < H; ++h) {
-    const size_t o = (((size_t)b * H + h) * S + i) * DH;
-    if (kToTokens)
-      copy_row<DH>(dst + tok + h * DH, src + o, lane);
-    else
-      copy_row<DH>(dst + o, src + tok + h * DH, lane);
+  for (int h0 = 0; h0 < H; h0 += kRows * kBatch) {
+    uint4 x[kBatch];
+#pragma unroll
+    for (int p = 0; p < kBatch; ++p) {
+      const int h = h0 + p * kRows + rsel;
+      const size_t o = (((size_t)b * H + h) * S + i) * DH + sub * 8;
+      if (h < H) x[p] = *reinterpret_cast<const uint4*>(src + (kToTokens ? o : tok + (size_t)h * DH + sub * 8));
+    }
+#pragma unroll
+    for (int p = 0; p < kBatch; ++p) {
+      const int h = h0 + p * kRows + rsel;
+      const size_t o = (((size_t)b * H + h) * S + i) * DH + sub * 8;
+      if (h < H) *reinterpret_cast<uint4*>(dst + (kToTokens ? tok + (size_t)h * DH + sub * 8 : o)) = x[p];
+    }
   }
 }
 
