@@ -1083,6 +1083,27 @@ def run_train_reference_arm(args, cfg):
     print(json.dumps(line), flush=True)
 
 
+def run_plan_only(args, cfg):
+    """The prepass alone on one GPU: each kind's tile plan rebuilt from the
+    workload's device batch, mean CUDA-event time per call (not a bench line)."""
+    import torch
+    dev = torch.device("cuda", 0)
+    wl = Workload(cfg, 1000, dev)
+    for _ in range(args.warmup):
+        for k in wl.kinds:
+            wl.rebuild_plan(k)
+    out = {}
+    for k in wl.kinds:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            wl.rebuild_plan(k)
+        e1.record()
+        torch.cuda.synchronize()
+        out[KIND_NAMES[k["kind"]]] = e0.elapsed_time(e1) / args.steps * 1000
+    print(json.dumps({"workload": cfg["name"], "prepass_us_per_call": out}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1102,6 +1123,9 @@ def main():
                     help="timed steps of the training-step record")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the workload's batch size (profiling runs)")
+    ap.add_argument("--plan-only", action="store_true",
+                    help="attention workloads, one GPU: only the prepass (rt_build_tile_plan of each kind, "
+                         "--steps times after --warmup), CUDA-event time per kind; for profiling runs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1111,6 +1135,8 @@ def main():
         cfg["name"] = cfg["name"].replace("_b%d_" % CONFIGS[args.config]["B"], "_b%d_" % args.batch)
     if cfg.get("train"):
         (run_train_reference_arm if args.impl == "reference" else run_train_arm)(args, cfg)
+    elif args.plan_only:
+        run_plan_only(args, cfg)
     elif args.impl == "reference":
         run_reference_arm(args, cfg)
     else:
