@@ -787,9 +787,9 @@ class TrainRun:
     cells, a replica with the same initial weights on every rank, and a
     TrainStep whose gradient buckets are all-reduced over NCCL (reduce=True)
     or kept local (reduce=False, the single-GPU step on the same device).
-    graph=True (steps without an all-reduce) records the whole step as one
-    CUDA graph and replays it: the cells are static tensors that a new batch
-    is copied into."""
+    graph=True records the step as CUDA graphs and replays them (one graph on
+    one GPU; with an all-reduce, two graphs with the exchange between them):
+    the cells are static tensors that a new batch is copied into."""
 
     def __init__(self, cfg, rank, dev, reduce=True, graph=False):
         import torch
@@ -874,14 +874,14 @@ def measure_train(cfg, steps, warmup, world, rank, local):
     solo_ms, _, _ = solo.timed(steps, world)
     del solo
     torch.cuda.empty_cache()
-    graph_ms = None
-    if world == 1:  # the same step recorded once as a CUDA graph and replayed
-        gr = TrainRun(cfg, rank, dev, reduce=False, graph=True)
-        for _ in range(warmup):
-            gr()
-        graph_ms, _, _ = gr.timed(steps, world)
-        del gr
-        torch.cuda.empty_cache()
+    # the same data-parallel step replayed from CUDA graphs (one graph on one
+    # GPU; two around the all-reduce on several)
+    gr = TrainRun(cfg, rank, dev, reduce=True, graph=True)
+    for _ in range(warmup):
+        gr()
+    graph_ms, graph_exposed_ms, _ = gr.timed(steps, world, finish_events=world > 1)
+    del gr
+    torch.cuda.empty_cache()
     status = device_status(reset=True)
     if status != 0 or not math.isfinite(loss_val):
         raise RuntimeError(f"training step: device status {status}, loss {loss_val}")
@@ -892,7 +892,9 @@ def measure_train(cfg, steps, warmup, world, rank, local):
                                   f"in {n_buckets} buckets, launched from post-accumulate hooks during backward",
                           "exposed_ms_per_step": exposed_ms},
             "ms_per_step_without_allreduce": solo_ms,
-            "ms_per_step_cuda_graph": graph_ms,
+            "cuda_graph": {"ms_per_step": graph_ms, "tokens_per_s": world * tokens / (graph_ms * 1e-3),
+                           "allreduce_exposed_ms_per_step": graph_exposed_ms,
+                           "graphs": 1 if world == 1 else 2},
             "efficiency_vs_1gpu": solo_ms / dp_ms,
             "replica_param_checksum_rel_spread": spread, "final_loss": loss_val}
 
@@ -903,8 +905,8 @@ def run_train_arm(args, cfg):
     from tributary_b200.train import build_masks
     world, rank, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
-    graph = world == 1 and not args.no_graph  # one GPU: the step replays from a CUDA graph
-    run = TrainRun(cfg, rank, dev, reduce=not graph, graph=graph)
+    graph = not args.no_graph  # the step replays from CUDA graphs (two around the all-reduce on N > 1)
+    run = TrainRun(cfg, rank, dev, graph=graph)
     for _ in range(args.warmup):
         run()
     barrier(world)
@@ -913,7 +915,7 @@ def run_train_arm(args, cfg):
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
-    step_ms, exposed_ms, loss = run.timed(args.steps, world, finish_events=not graph)
+    step_ms, exposed_ms, loss = run.timed(args.steps, world, finish_events=not graph or world > 1)
     clocks = sampler.stop()
     # end to end: every step copies its cell arrays from pinned host memory and reads the loss back
     h2d = sum(v.numel() * v.element_size() for v in run.host.values())
@@ -947,7 +949,9 @@ def run_train_arm(args, cfg):
                        "optimizer": "muon (2-D weights) + adamw, global-norm clip 1.0",
                        "l2": "working set (activations of 48 sublayers) far above L2",
                        "parallelism": (f"dp{world}: NCCL all-reduce (average) of fp32 gradients in "
-                                       f"{len(run.step.buckets.buffers)} buckets, overlapped with backward")
+                                       f"{len(run.step.buckets.buffers)} buckets, "
+                                       + ("between the backward and update graphs" if graph
+                                          else "overlapped with backward"))
                                       if world > 1 else "dp1: one GPU, no collective",
                        "cuda_graph": graph},
             "allreduce_exposed_ms_per_step": exposed_ms,
@@ -1118,7 +1122,7 @@ def main():
     ap.add_argument("--no-sweep", action="store_true",
                     help="attention workloads: skip the B=32 S=1024 record and the length x density sweep")
     ap.add_argument("--no-graph", action="store_true",
-                    help="--config d on one GPU: run the step eagerly instead of replaying a CUDA graph")
+                    help="--config d: run the step eagerly instead of replaying CUDA graphs")
     ap.add_argument("--train-steps", type=int, default=10,
                     help="timed steps of the training-step record")
     ap.add_argument("--batch", type=int, default=None,

@@ -1,7 +1,10 @@
-"""The training step recorded as one CUDA graph (TrainStep.capture / replay:
+"""The training step recorded as CUDA graphs (TrainStep.capture / replay:
 tile plans, forward, loss, backward, clipping, Muon and AdamW) against the
 same steps run eagerly from the same weights and batch, and a replay that
-reads new cell values copied into the captured tensors."""
+reads new cell values copied into the captured tensors. Both forms: one graph
+for the whole step, and the two graphs (forward + backward, then the update)
+that steps with a gradient all-reduce use, the exchange running between
+them."""
 import numpy as np
 import pytest
 import torch
@@ -21,7 +24,8 @@ def _fresh(cfg):
     return model, TrainStep(model, muon_lr=0.01, adamw_lr=1e-3, capturable=True)
 
 
-def test_graph_replay_matches_eager_steps(cuda_lib):
+@pytest.mark.parametrize("split", [False, True], ids=["one_graph", "two_graphs"])
+def test_graph_replay_matches_eager_steps(cuda_lib, split):
     from tributary_b200.attention import device_status
     from tributary_b200.train import build_masks
     cfg = tiny_config(d_model=128, n_heads=2, d_head=64, d_ff=256, n_layers=2)
@@ -32,17 +36,21 @@ def test_graph_replay_matches_eager_steps(cuda_lib):
     eager = [float(s1(c, build_masks(c, KINDS), col, cat)) for _ in range(7)]
 
     m2, s2 = _fresh(cfg)
-    s2.capture(c, col, cat, KINDS, warmup=3)  # three eager steps, then the recorded one
+    s2.capture(c, col, cat, KINDS, warmup=3, split=split)  # three eager steps, then the recorded one
+    assert (s2.graph_update is not None) == split
     replayed = [float(s2.replay()) for _ in range(4)]
     torch.cuda.synchronize()
     assert device_status() == 0
-    # dQ adds its partials in an order the memory system picks: replays match
-    # the eager steps to rounding, not bit for bit
-    np.testing.assert_allclose(replayed, eager[3:], rtol=1e-2)
+    # dQ adds its partials in an order the memory system picks, so no two runs
+    # are bit-identical, and seven training steps grow those last-bit
+    # differences to about 1 % of the loss. A graph that replays stale plans,
+    # skips an update or reads the wrong buffers is far off from step one.
+    np.testing.assert_allclose(replayed, eager[3:], rtol=3e-2)
+    assert replayed[-1] < replayed[0] - 0.5 * (eager[3] - eager[6])  # the replays keep training
     with torch.no_grad():
         num = sum(float((p - q).float().norm() ** 2) for p, q in zip(m1.parameters(), m2.parameters()))
         den = sum(float(q.float().norm() ** 2) for q in m1.parameters())
-    assert (num / den) ** 0.5 < 1e-2
+    assert (num / den) ** 0.5 < 3e-2
 
     # the graph reads the captured cell tensors in place: new values change the loss
     before = float(s2.replay())

@@ -117,6 +117,9 @@ class GradBuckets:
         self.works = []
         self.launch_error = None
         self.launched = [False] * len(groups)
+        # defer: the hooks only count (a backward recorded into a CUDA graph
+        # launches no collective; reduce_all() exchanges the buckets after it)
+        self.defer = False
 
     @property
     def bucket_sizes(self):
@@ -138,7 +141,7 @@ class GradBuckets:
         if self.launched[i]:
             return
         self.launched[i] = True
-        if self.world > 1:
+        if self.world > 1 and not self.defer:
             op = dist.ReduceOp.AVG if self.avg else dist.ReduceOp.SUM
             try:
                 self.works.append(dist.all_reduce(self.buffers[i], op=op, group=self.group, async_op=True))
@@ -184,6 +187,15 @@ class GradBuckets:
         if self.world > 1 and not self.avg:
             for buf in self.buffers:
                 buf.div_(self.world)
+
+    def reduce_all(self, timeout_s: float | None = None):
+        """All-reduce every bucket now and wait, as finish() does: the
+        exchange between the two graphs of a step recorded with deferred
+        hooks."""
+        self.launched = [False] * len(self.buffers)
+        self.works = []
+        self.launch_error = None
+        self.finish(timeout_s)
 
     def global_norm(self) -> torch.Tensor:
         return torch.linalg.vector_norm(torch.stack([torch.linalg.vector_norm(b) for b in self.buffers]))
@@ -263,6 +275,7 @@ class TrainStep:
         self.max_grad_norm = max_grad_norm
         self.autocast = autocast and dev.type == "cuda"
         self.graph = None
+        self.graph_update = None
         self.graph_loss = None
 
     def __call__(self, cells, masks, col_table, cat_table) -> torch.Tensor:
@@ -271,18 +284,23 @@ class TrainStep:
         self.steps += 1
         return self._step(cells, masks, col_table, cat_table)
 
-    def capture(self, cells, col_table, cat_table, kinds, warmup: int = 3) -> None:
-        """Record one whole step -- the tile plans of ``kinds`` built from the
-        device tensors of ``cells``, forward, loss, backward, clipping and both
-        optimizer updates -- as a CUDA graph, after ``warmup`` eager steps on a
+    def capture(self, cells, col_table, cat_table, kinds, warmup: int = 3, split: bool | None = None) -> None:
+        """Record the step as CUDA graphs, after ``warmup`` eager steps on a
         side stream (which also create the optimizer state). Every replay()
         then reads ``cells`` in place: copy each new batch into those tensors
-        first. Needs capturable=True; steps without a cross-rank collective
-        only (the gradient all-reduce stays eager)."""
+        first. Needs capturable=True.
+
+        One GPU: one graph holds the whole step -- the tile plans of ``kinds``
+        built from ``cells``, forward, loss, backward, clipping and both
+        optimizer updates. Several GPUs (or ``split``): the gradient
+        all-reduce stays outside, so the step is two graphs -- plans, forward,
+        loss and backward into the buckets, then clipping and the updates --
+        with reduce_all() between them on the host (the exchange no longer
+        overlaps the backward, in exchange for no per-kernel launch cost)."""
         if not self.capturable:
             raise ValueError("TrainStep(capturable=True) is needed for capture()")
-        if self.buckets.world > 1:
-            raise ValueError("capture() covers steps without a gradient all-reduce")
+        if split is None:
+            split = self.buckets.world > 1
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
@@ -291,9 +309,21 @@ class TrainStep:
         torch.cuda.current_stream().wait_stream(side)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            loss = self._step(cells, build_masks(cells, kinds), col_table, cat_table)
-        self.graph, self.graph_loss = graph, loss
+        if not split:
+            with torch.cuda.graph(graph):
+                loss = self._step(cells, build_masks(cells, kinds), col_table, cat_table)
+            self.graph, self.graph_update, self.graph_loss = graph, None, loss
+            return
+        self.buckets.defer = True
+        try:
+            with torch.cuda.graph(graph):
+                loss = self._forward_backward(cells, build_masks(cells, kinds), col_table, cat_table)
+        finally:
+            self.buckets.defer = False
+        update = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(update, pool=graph.pool()):
+            self._update()
+        self.graph, self.graph_update, self.graph_loss = graph, update, loss
 
     def replay(self) -> torch.Tensor:
         """One captured step on the current contents of the captured cells;
@@ -304,14 +334,35 @@ class TrainStep:
             self.heartbeat.step(self.steps)
         self.steps += 1
         self.graph.replay()
+        if self.graph_update is not None:
+            if self.finish_events is not None:
+                ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                ev[0].record()
+                self.buckets.reduce_all(self.allreduce_timeout_s)
+                ev[1].record()
+                self.finish_events.append(ev)
+            else:
+                self.buckets.reduce_all(self.allreduce_timeout_s)
+            self.graph_update.replay()
         return self.graph_loss
 
-    def _step(self, cells, masks, col_table, cat_table) -> torch.Tensor:
+    def _forward_backward(self, cells, masks, col_table, cat_table) -> torch.Tensor:
         self.buckets.zero()
         with torch.autocast("cuda", dtype=torch.bfloat16, enabled=self.autocast):
             out = self.model(cells, masks, col_table, cat_table)
             loss = self.model.loss(out, cells, cat_table)
         loss.backward()
+        return loss.detach()
+
+    def _update(self) -> None:
+        norm = self.buckets.global_norm()
+        clip = torch.clamp(self.max_grad_norm / (norm + 1e-6), max=1.0)
+        torch._foreach_mul_(self.buckets.buffers, clip)
+        self.muon.step()
+        self.adamw.step()
+
+    def _step(self, cells, masks, col_table, cat_table) -> torch.Tensor:
+        loss = self._forward_backward(cells, masks, col_table, cat_table)
         if self.finish_events is not None:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             ev[0].record()
@@ -320,12 +371,8 @@ class TrainStep:
             self.finish_events.append(ev)
         else:
             self.buckets.finish(self.allreduce_timeout_s)
-        norm = self.buckets.global_norm()
-        clip = torch.clamp(self.max_grad_norm / (norm + 1e-6), max=1.0)
-        torch._foreach_mul_(self.buckets.buffers, clip)
-        self.muon.step()
-        self.adamw.step()
-        return loss.detach()
+        self._update()
+        return loss
 
 
 def build_masks(meta: dict, kinds, max_rows: int | None = None):
