@@ -100,6 +100,18 @@ def test_argument_validation_before_device_work(lib):
     assert lib.rt_attention_bwd(fake, fake, fake, fake, fake, fake, 1, 1, 128, 64, 1.0,
                                 ctypes.byref(plan), fake, fake, fake, fake, ws - 256,
                                 None) == _lib.RT_ERR_WORKSPACE
+    # the sublayer backward (token-order outputs): same checks, plus its own pointers
+    def bwd_qkv(scale=1.0, head_dim=64, perm=fake, dtau=fake, ws_bytes=ws):
+        return lib.rt_attention_bwd_qkv(fake, fake, fake, fake, fake, fake, 1, 1, 128, head_dim, scale,
+                                        ctypes.byref(plan), perm, fake, fake, fake, fake, dtau, fake,
+                                        ws_bytes, None)
+    assert bwd_qkv(head_dim=48) == _lib.RT_ERR_UNSUPPORTED
+    assert bwd_qkv(scale=0.0) == _lib.RT_ERR_INVALID_ARGUMENT
+    assert bwd_qkv(perm=None) == _lib.RT_ERR_INVALID_ARGUMENT
+    assert bwd_qkv(dtau=odd) == _lib.RT_ERR_INVALID_ARGUMENT
+    assert bwd_qkv(ws_bytes=ws - 256) == _lib.RT_ERR_WORKSPACE
+    assert lib.rt_attention_bwd_qkv(None, None, None, None, None, None, 0, 1, 128, 64, 1.0, ctypes.byref(empty),
+                                    None, None, None, None, None, None, None, 0, None) == 0
 
 
 def test_xla_ffi_handlers_need_jax():
