@@ -15,6 +15,10 @@
 //   gradients: dK and dV accumulate in TMEM and are written once, while dQ
 //   partials are reduce-added (TMA) into an fp32 workspace accumulator that
 //   dq_convert_kernel scales and rounds. dQ is reproducible to fp32 rounding.
+//   rt_attention_bwd_qkv runs the same kernel with token-order outputs
+//   (TokenGrads): dK and dV leave its epilogue through the k normalisation's
+//   Jacobian and the scatter to token order, and dq_qkv_kernel does the same
+//   for dQ.
 // - rt_attention_bwd_noalloc: dkdv_kernel (k2q lists, thread = key) and
 //   dq_kernel (q2k lists, thread = query). Each output element is written once
 //   by one CTA, so all three gradients are bit-reproducible; the only scratch

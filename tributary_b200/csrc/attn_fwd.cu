@@ -128,8 +128,10 @@ __global__ void __launch_bounds__(256) attn_fwd_rowfix_kernel(const uint16_t* __
 //                K / V tiles (TMA) and, for partial tiles, the 2 KB block of
 //                mask words (bulk copy) into a 4-stage ring; per item, Q into
 //                one of two slots
-//   warp 1       MMA issuer: S_g = Q K_g^T into S buffer g % 3, O += P_g V_g
-//                into the item's O buffer (two, alternating by item)
+//   warp 1       PV issuer: O += P_g V_g into the item's O buffer (two,
+//                alternating by item), in tile order
+//   warp 18      S issuer: S_g = Q K_g^T into S buffer g % 3 once PV_{g-3},
+//                which reads P_{g-3} from that buffer, has completed
 //   warps 2..5   epilogue warpgroup: diagonal logits two items ahead, then
 //                O / l -> bf16 and lse per item
 //   warps 6..17  softmax: three sets of 4 warps (one per TMEM lane quadrant);
