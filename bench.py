@@ -183,8 +183,8 @@ class Workload:
 
     def launches_per_step(self):
         # prepass: set-up (perm check, fk packing), tile mask, tile list;
-        # forward: main kernel + row fix-up; backward: row stats, dK/dV/dQ, dQ conversion
-        return sum(3 + 2 + 3 for _ in range(4))
+        # forward: one kernel; backward: row stats, dK/dV/dQ, dQ conversion
+        return sum(3 + 1 + 3 for _ in range(4))
 
     def rebuild_plan(self, k):
         lib = self.rt._lib

@@ -1,7 +1,7 @@
 // Forward masked attention on sm_100a (tcgen05 + TMA), one 128-query tile of
 // one (batch, head) per CTA, iterating only the live key tiles of the plan
-// (attn_fwd_kernel), followed by an exact fp32 fix-up of the rare rows it
-// marks (attn_fwd_rowfix_kernel).
+// (attn_fwd_kernel); the rare rows outside its exponent range are recomputed
+// exactly in fp32 by the epilogue warp that finds them (fix_row).
 //
 // Replaces confluence/confluence/layers.py:83-94: s = q k^T * scale,
 // where(mask, s, -1e9), softmax, p v. Masked elements are excluded exactly
@@ -26,97 +26,79 @@ constexpr int kMaxTiles = 65536 / RT_TILE;  // tiles per row of the plan (seq_le
 static_assert(kMaxTiles <= 512, "tile list must fit in shared memory");
 
 // ---------------------------------------------------------------------------
-// Exact fallback for the rare rows the main kernel marks (lse = NaN): their
-// logit spread exceeded the range of the diagonal reference. One warp per
-// marked row recomputes it in fp32 on the CUDA cores with an online max:
-// lanes take 32 keys at a time, o is spread over the lanes (DH/32 columns
-// each). In the common case no row is marked and the kernel only scans lse.
+// Exact fallback for the rare rows the main kernel cannot take (their logit
+// spread exceeds the range of the diagonal reference): the epilogue warp that
+// finds one recomputes it on the spot, the whole warp in fp32 on the CUDA
+// cores with an online max. Lanes take 32 keys at a time, o is spread over
+// the lanes (DH/32 columns each), and q is read from cache for every dot
+// product instead of being held in registers, so the path costs the main
+// kernel no registers. In the common case it never runs.
 // ---------------------------------------------------------------------------
 template <int DH>
-__global__ void __launch_bounds__(256) attn_fwd_rowfix_kernel(const uint16_t* __restrict__ qg,
-                                                              const uint16_t* __restrict__ kg,
-                                                              const uint16_t* __restrict__ vg, const rt_tile_plan plan,
-                                                              int H, int S, float c, uint16_t* __restrict__ out,
-                                                              float* __restrict__ lse) {
+__device__ __noinline__ void fix_row(long long r, const uint16_t* __restrict__ qg, const uint16_t* __restrict__ kg,
+                                     const uint16_t* __restrict__ vg, const rt_tile_plan& plan, int H, int S,
+                                     float c, uint16_t* __restrict__ out, float* __restrict__ lse) {
   constexpr int kPer = DH / 32;  // output columns per lane
   const int lane = threadIdx.x & 31;
-  const long long total = (long long)plan.batch * H * S;
-  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
   const int T = plan.tiles;
-  for (long long base = ((long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 32; base < total;
-       base += warps * 32) {
-    const long long mine = base + lane;
-    uint32_t todo = __ballot_sync(0xFFFFFFFFu, mine < total && isnan(lse[mine]));
-    while (todo) {
-      const int src = __ffs(todo) - 1;
-      todo &= todo - 1;
-      const long long r = base + src;
-      const int bh = (int)(r / S), i = (int)(r % S);
-      const int b = bh / H, qt = i / RT_TILE, ri = i % RT_TILE;
-      float qf[DH];
+  const int bh = (int)(r / S), i = (int)(r % S);
+  const int b = bh / H, qt = i / RT_TILE, ri = i % RT_TILE;
+  const uint32_t* qrow = reinterpret_cast<const uint32_t*>(qg + (size_t)r * DH);
+  float m = -INFINITY, l = 0.f, o[kPer];
 #pragma unroll
-      for (int d = 0; d < DH; d += 2) {
-        const float2 f = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(qg + (size_t)r * DH + d));
-        qf[d] = f.x;
-        qf[d + 1] = f.y;
+  for (int e = 0; e < kPer; ++e) o[e] = 0.f;
+  const int lb = plan.q2k_ptr[b * T + qt], le = plan.q2k_ptr[b * T + qt + 1];
+  for (int t = lb; t < le; ++t) {
+    const int ent = plan.q2k_idx[t];
+    const int kt = ent & 0x7FFFFFFF;
+    const uint32_t* mrow = plan.tile_masks + ((((size_t)b * T + qt) * T + kt) * RT_TILE + ri) * 4;
+    for (int ch = 0; ch < 4; ++ch) {
+      const int j = kt * RT_TILE + ch * 32 + lane;
+      const bool live = j < S && (ent < 0 || ((mrow[ch] >> lane) & 1u));
+      float sc = -INFINITY;
+      if (live) {
+        float acc = 0.f;
+        const uint32_t* krow = reinterpret_cast<const uint32_t*>(kg + ((size_t)bh * S + j) * DH);
+        for (int d = 0; d < DH / 2; ++d) {
+          const float2 qf = unpack_bf16x2(__ldg(qrow + d));
+          const float2 kf = unpack_bf16x2(__ldg(krow + d));
+          acc = fmaf(qf.x, kf.x, fmaf(qf.y, kf.y, acc));
+        }
+        sc = acc * c;
       }
-      float m = -INFINITY, l = 0.f, o[kPer];
+      float cm = sc;
 #pragma unroll
-      for (int e = 0; e < kPer; ++e) o[e] = 0.f;
-      const int lb = plan.q2k_ptr[b * T + qt], le = plan.q2k_ptr[b * T + qt + 1];
-      for (int t = lb; t < le; ++t) {
-        const int ent = plan.q2k_idx[t];
-        const int kt = ent & 0x7FFFFFFF;
-        const uint32_t* mrow = plan.tile_masks + ((((size_t)b * T + qt) * T + kt) * RT_TILE + ri) * 4;
-        for (int ch = 0; ch < 4; ++ch) {
-          const int j = kt * RT_TILE + ch * 32 + lane;
-          const bool live = j < S && (ent < 0 || ((mrow[ch] >> lane) & 1u));
-          float sc = -INFINITY;
-          if (live) {
-            float acc = 0.f;
-            const uint16_t* krow = kg + ((size_t)bh * S + j) * DH;
+      for (int off = 16; off > 0; off >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xFFFFFFFFu, cm, off));
+      const float mn = fmaxf(m, cm);
+      if (mn == -INFINITY) continue;
+      const float alpha = m == -INFINITY ? 0.f : exp2f(m - mn);
+      const float p = live ? exp2f(sc - mn) : 0.f;
+      float ps = p;
 #pragma unroll
-            for (int d = 0; d < DH; d += 2) {
-              const float2 kf = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(krow + d));
-              acc = fmaf(qf[d], kf.x, fmaf(qf[d + 1], kf.y, acc));
-            }
-            sc = acc * c;
-          }
-          float cm = sc;
+      for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xFFFFFFFFu, ps, off);
+      l = l * alpha + ps;
 #pragma unroll
-          for (int off = 16; off > 0; off >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xFFFFFFFFu, cm, off));
-          const float mn = fmaxf(m, cm);
-          if (mn == -INFINITY) continue;
-          const float alpha = m == -INFINITY ? 0.f : exp2f(m - mn);
-          const float p = live ? exp2f(sc - mn) : 0.f;
-          float ps = p;
+      for (int e = 0; e < kPer; ++e) o[e] *= alpha;
+      for (int src2 = 0; src2 < 32; ++src2) {
+        const float pj = __shfl_sync(0xFFFFFFFFu, p, src2);
+        const int jj = kt * RT_TILE + ch * 32 + src2;
+        if (pj != 0.f) {
+          const uint16_t* vrow = vg + ((size_t)bh * S + jj) * DH + lane * kPer;
 #pragma unroll
-          for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xFFFFFFFFu, ps, off);
-          l = l * alpha + ps;
-#pragma unroll
-          for (int e = 0; e < kPer; ++e) o[e] *= alpha;
-          for (int src2 = 0; src2 < 32; ++src2) {
-            const float pj = __shfl_sync(0xFFFFFFFFu, p, src2);
-            const int jj = kt * RT_TILE + ch * 32 + src2;
-            if (pj != 0.f) {
-              const uint16_t* vrow = vg + ((size_t)bh * S + jj) * DH + lane * kPer;
-#pragma unroll
-              for (int e = 0; e < kPer; ++e) o[e] = fmaf(pj, __uint_as_float((uint32_t)vrow[e] << 16), o[e]);
-            }
-          }
-          m = mn;
+          for (int e = 0; e < kPer; ++e) o[e] = fmaf(pj, __uint_as_float((uint32_t)vrow[e] << 16), o[e]);
         }
       }
-      const float inv_l = l > 0.f ? 1.f / l : 0.f;
-      uint16_t* orow = out + (size_t)r * DH + lane * kPer;
-#pragma unroll
-      for (int e = 0; e < kPer; ++e) {
-        const __nv_bfloat16 bv = __float2bfloat16_rn(o[e] * inv_l);
-        orow[e] = *reinterpret_cast<const uint16_t*>(&bv);
-      }
-      if (lane == 0) lse[r] = l > 0.f ? (m + log2f(l)) * 0.6931471805599453f : -INFINITY;
+      m = mn;
     }
   }
+  const float inv_l = l > 0.f ? 1.f / l : 0.f;
+  uint16_t* orow = out + (size_t)r * DH + lane * kPer;
+#pragma unroll
+  for (int e = 0; e < kPer; ++e) {
+    const __nv_bfloat16 bv = __float2bfloat16_rn(o[e] * inv_l);
+    orow[e] = *reinterpret_cast<const uint16_t*>(&bv);
+  }
+  if (lane == 0) lse[r] = l > 0.f ? (m + log2f(l)) * 0.6931471805599453f : -INFINITY;
 }
 
 // ---------------------------------------------------------------------------
@@ -143,7 +125,7 @@ __global__ void __launch_bounds__(256) attn_fwd_rowfix_kernel(const uint16_t* __
 // or O rescaling is needed (softmax is invariant to the reference). A row
 // whose terms leave the safe range (row sum >= 2^100 or |O| >= 2^120, i.e. a
 // logit spread above about (100 + kRefShift)/c, impossible for L2-normalised
-// q, k) is marked with lse = NaN and recomputed by attn_fwd_rowfix_kernel.
+// q, k) is recomputed exactly by the epilogue warp that finds it (fix_row).
 // TMEM (512 columns): S buffers [0,128), [128,256), [256,384) fp32 with P_g
 // written as bf16 pairs over columns [0,64) of its buffer, O buffers
 // [384, 384+DH) and [384+DH, 384+2DH).
@@ -223,8 +205,8 @@ template <int DH>
 __global__ void __launch_bounds__(kMainThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const uint16_t* __restrict__ qg,
-                    const uint16_t* __restrict__ kg, const rt_tile_plan plan, int H, int S, float scale_log2,
-                    uint16_t* __restrict__ out, float* __restrict__ lse) {
+                    const uint16_t* __restrict__ kg, const uint16_t* __restrict__ vg, const rt_tile_plan plan,
+                    int H, int S, float scale_log2, uint16_t* __restrict__ out, float* __restrict__ lse) {
   using C = MainCfg<DH>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -490,6 +472,15 @@ __global__ void __launch_bounds__(kMainThreads, 1)
         lse[(size_t)bh * S + qrow] =
             bad ? __int_as_float(0x7FC00000) : (sd * c + kRefShift + __log2f(l)) * 0.6931471805599453f;
       }
+      // rows outside the diagonal reference's range: the whole warp
+      // recomputes each one exactly (it overwrites the NaN lse above)
+      uint32_t todo = __ballot_sync(0xFFFFFFFFu, bad && qrow < S);
+      __syncwarp();
+      while (todo) {
+        const int src = __ffs(todo) - 1;
+        todo &= todo - 1;
+        fix_row<DH>((long long)bh * S + ic.qt * RT_TILE + quad * 32 + src, qg, kg, vg, plan, H, S, c, out, lse);
+      }
     }
     tc_fence_before();
   } else {
@@ -600,12 +591,9 @@ int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H
   const int sms = dev >= 0 && dev < 64 ? num_sms[dev] : 148;
   const long long items = (long long)B * H * plan.tiles;
   const int grid = (int)std::min<long long>(items, sms);
-  attn_fwd_kernel<DH><<<grid, kMainThreads, M::kDynSmem, stream>>>(tq, tk, tv, q, k, plan, H, S, scale_log2, o, lse);
-  if (int st = check_launch("attn_fwd_kernel launch")) return st;
-  const long long rows = (long long)B * H * S;
-  const int fix_blocks = (int)std::min<long long>((rows + 255) / 256, 4LL * (dev >= 0 && dev < 64 ? num_sms[dev] : 148));
-  attn_fwd_rowfix_kernel<DH><<<fix_blocks, 256, 0, stream>>>(q, k, v, plan, H, S, scale_log2, o, lse);
-  return check_launch("attn_fwd_rowfix_kernel launch");
+  attn_fwd_kernel<DH><<<grid, kMainThreads, M::kDynSmem, stream>>>(tq, tk, tv, q, k, v, plan, H, S, scale_log2, o,
+                                                                    lse);
+  return check_launch("attn_fwd_kernel launch");
 }
 
 }  // namespace fwd
