@@ -251,6 +251,8 @@ __global__ void __launch_bounds__(256) row_stats_kernel(const uint16_t* __restri
                                                         float* __restrict__ stats, uint16_t* __restrict__ aux,
                                                         float* __restrict__ dq_acc, float inv_scale, int S, int Sp,
                                                         long long rows_padded) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   constexpr int kLanesPerRow = DH / 8;
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long prow = gid / kLanesPerRow;
@@ -752,6 +754,8 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
                 const __grid_constant__ CUtensorMap tm_aux, const rt_tile_plan plan, int H, int S, float scale,
                 float scale_log2, uint16_t* __restrict__ dk, uint16_t* __restrict__ dv,
                 const __grid_constant__ CUtensorMap tm_acc, const TokenGrads tg) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   using C = Cfg<DH>;
   constexpr int kST0 = 0, kDPT = 256, kDV = 384, kDK = 384 + DH;
   extern __shared__ uint8_t smem_raw[];
@@ -1148,6 +1152,8 @@ __global__ void __launch_bounds__(kThreadsFused, 1)
 template <int DH>
 __global__ void __launch_bounds__(256) dq_convert_kernel(const float* __restrict__ dq_acc, uint16_t* __restrict__ dq,
                                                          long long rows, int S, int Sp, float scale) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;  // 8 elements each
   const long long row = gid / (DH / 8);
   if (row >= rows) return;
@@ -1168,6 +1174,8 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(const float* __restrict
 template <int DH>
 __global__ void __launch_bounds__(256) dq_qkv_kernel(const float* __restrict__ dq_acc, long long rows, int H, int S,
                                                      int Sp, float scale, const TokenGrads tg) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   constexpr int kLanes = DH / 8;
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long row = gid / kLanes;
@@ -1240,31 +1248,28 @@ int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16
   // fused path: the statistics ride in the MMAs as -lse / scale, so scale > 0
   const bool fused = dq_acc != nullptr && aux != nullptr && scale > 0.f && scale < 3.0e38f;
   // fused path: operand rows and the zeroed dQ accumulator; otherwise the statistics
-  row_stats_kernel<DH><<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
-      o, d_o, lse, fused ? nullptr : stats, fused ? aux : nullptr, fused ? dq_acc : nullptr,
-      fused ? 1.0f / scale : 0.f, S, Sp, rows_padded);
-  if (int st = check_launch("row_stats_kernel launch")) return st;
+  if (int st = launch_pdl("row_stats_kernel launch", row_stats_kernel<DH>, dim3((unsigned)((threads + 255) / 256)),
+                          dim3(256), 0, stream, o, d_o, lse, fused ? nullptr : stats, fused ? aux : nullptr,
+                          fused ? dq_acc : nullptr, fused ? 1.0f / scale : 0.f, S, Sp, rows_padded))
+    return st;
   const float scale_log2 = scale * 1.4426950408889634f;
   dim3 grid(plan.tiles, H, B);
   if (fused) {  // one pass for dK, dV and dQ
     CUtensorMap tacc, taux;
     if (make_acc_tensor_map(&tacc, dq_acc, rows_padded, DH) != RT_OK) return RT_ERR_CUDA;
     if (make_aux_tensor_map(&taux, aux, rows_padded) != RT_OK) return RT_ERR_CUDA;
-    if (tg.dqkv != nullptr)
-      dkdvq_kernel<DH, true><<<grid, kThreadsFused, C::kDynSmemFused, stream>>>(tq, tk, tv, tdo, taux, plan, H, S,
-                                                                             scale, scale_log2, dk, dv, tacc, tg);
-    else
-      dkdvq_kernel<DH, false><<<grid, kThreadsFused, C::kDynSmemFused, stream>>>(tq, tk, tv, tdo, taux, plan, H, S,
-                                                                              scale, scale_log2, dk, dv, tacc, tg);
-    if (int st = check_launch("dkdvq_kernel launch")) return st;
+    if (int st = launch_pdl("dkdvq_kernel launch", tg.dqkv != nullptr ? dkdvq_kernel<DH, true> : dkdvq_kernel<DH, false>,
+                            grid, dim3(kThreadsFused), C::kDynSmemFused, stream, tq, tk, tv, tdo, taux, plan, H, S,
+                            scale, scale_log2, dk, dv, tacc, tg))
+      return st;
     const long long rows = (long long)B * H * S;
     const long long cthreads = rows * (DH / 8);
-    if (tg.dqkv != nullptr) {
-      dq_qkv_kernel<DH><<<(unsigned)((cthreads + 255) / 256), 256, 0, stream>>>(dq_acc, rows, H, S, Sp, scale, tg);
-      return check_launch("dq_qkv_kernel launch");
-    }
-    dq_convert_kernel<DH><<<(unsigned)((cthreads + 255) / 256), 256, 0, stream>>>(dq_acc, dq, rows, S, Sp, scale);
-    return check_launch("dq_convert_kernel launch");
+    const dim3 cgrid((unsigned)((cthreads + 255) / 256));
+    if (tg.dqkv != nullptr)
+      return launch_pdl("dq_qkv_kernel launch", dq_qkv_kernel<DH>, cgrid, dim3(256), 0, stream, dq_acc, rows, H, S, Sp,
+                        scale, tg);
+    return launch_pdl("dq_convert_kernel launch", dq_convert_kernel<DH>, cgrid, dim3(256), 0, stream, dq_acc, dq, rows,
+                      S, Sp, scale);
   }
   dkdv_kernel<DH><<<grid, kThreads, C::kDynSmem, stream>>>(tq, tk, tv, tdo, plan, H, S, scale, scale_log2,
                                                             stats, dk, dv);

@@ -207,6 +207,8 @@ __global__ void __launch_bounds__(kMainThreads, 1)
                     const __grid_constant__ CUtensorMap tm_v, const uint16_t* __restrict__ qg,
                     const uint16_t* __restrict__ kg, const uint16_t* __restrict__ vg, const rt_tile_plan plan,
                     int H, int S, float scale_log2, uint16_t* __restrict__ out, float* __restrict__ lse) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   using C = MainCfg<DH>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -591,9 +593,8 @@ int launch(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H
   const int sms = dev >= 0 && dev < 64 ? num_sms[dev] : 148;
   const long long items = (long long)B * H * plan.tiles;
   const int grid = (int)std::min<long long>(items, sms);
-  attn_fwd_kernel<DH><<<grid, kMainThreads, M::kDynSmem, stream>>>(tq, tk, tv, q, k, v, plan, H, S, scale_log2, o,
-                                                                    lse);
-  return check_launch("attn_fwd_kernel launch");
+  return launch_pdl("attn_fwd_kernel launch", attn_fwd_kernel<DH>, dim3(grid), dim3(kMainThreads), M::kDynSmem,
+                    stream, tq, tk, tv, q, k, v, plan, H, S, scale_log2, o, lse);
 }
 
 }  // namespace fwd

@@ -179,6 +179,14 @@ __device__ __forceinline__ void bulk_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
 
+// Programmatic dependent launch (launch_pdl in rt_internal.h). pdl_wait:
+// until the previous grid on the stream has completed and its writes are
+// visible; every kernel of the attention path calls it before its first global
+// access (a no-op for an ordinary launch). pdl_trigger: lets the next grid be
+// set up now; its own pdl_wait still holds it until this grid completes.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -16,6 +16,29 @@ inline int check_launch(const char* site) {
   return e == cudaSuccess ? RT_OK : cuda_failure(e, site);
 }
 
+// Launches a kernel of the attention path with programmatic stream
+// serialisation: the grid may be set up while the previous kernel on the
+// stream drains. Every such kernel begins with pdl_wait() (griddepcontrol.wait,
+// rt_device.cuh), which returns once the previous grid has completed and its
+// memory is visible, before the kernel's first global access; launched any
+// other way the wait is a no-op.
+template <typename... KernelArgs, typename... Args>
+int launch_pdl(const char* site, void (*kernel)(KernelArgs...), dim3 grid, dim3 block, size_t smem,
+               cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KernelArgs>(args)...);
+  return e == cudaSuccess ? RT_OK : cuda_failure(e, site);
+}
+
 int launch_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids, const int32_t* column_ids,
                            const uint8_t* is_padding, const uint8_t* fk_adj, int B, int S, int R,
                            int kind, const rt_tile_plan& plan, cudaStream_t stream);

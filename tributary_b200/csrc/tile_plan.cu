@@ -44,6 +44,8 @@ __global__ void __launch_bounds__(kSetupThreads) plan_setup_kernel(
     const uint16_t* __restrict__ perm, int B, int S, int32_t* __restrict__ flags, uint32_t* __restrict__ live,
     uint32_t* __restrict__ full, int tw, const uint8_t* __restrict__ fk_adj, int R, int WR, int transpose,
     uint32_t* __restrict__ fk_bits) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   if ((int)blockIdx.x < B) {
     __shared__ uint32_t bm[65536 / 32];
     __shared__ int dup;
@@ -126,6 +128,8 @@ __global__ void __launch_bounds__(kTileWarps * 32) tile_mask_kernel(
     const uint16_t* __restrict__ perm, const uint16_t* __restrict__ seq_row_ids,
     const int32_t* __restrict__ column_ids, const uint8_t* __restrict__ is_padding,
     const uint32_t* __restrict__ fk_bits, int S, int R, int WR, rt_tile_plan plan) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   constexpr bool kFk = KIND == RT_MASK_FEATURE || KIND == RT_MASK_NEIGHBOR;
   constexpr uint32_t kAll = 0xFFFFFFFFu;
   const int qt = blockIdx.y;
@@ -283,6 +287,8 @@ constexpr int kListSmemBytes = 96 * 1024;  // tile_list_kernel's staged bitmaps 
 constexpr int kListThreads = 512;
 
 __global__ void __launch_bounds__(kListThreads) tile_list_kernel(rt_tile_plan plan) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   const int T = plan.tiles;
   const int W = plan.words;
   const int b = blockIdx.x;
@@ -395,30 +401,26 @@ int launch_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids, co
   const uint32_t* fk_bits = needs_fk ? plan.fk_bits : nullptr;
   const long long fk_tasks = needs_fk ? (long long)B * WR * WR : 0;
   const int setup_blocks = B + (int)((fk_tasks + kSetupThreads / 32 - 1) / (kSetupThreads / 32));
-  plan_setup_kernel<<<setup_blocks, kSetupThreads, 0, stream>>>(perm, B, S, plan.nnz + 1, plan.live_bits,
-                                                                plan.full_bits, T * W, fk_adj, R, WR,
-                                                                kind == RT_MASK_NEIGHBOR ? 1 : 0, plan.fk_bits);
+  if (int st = launch_pdl("plan_setup_kernel launch", plan_setup_kernel, dim3(setup_blocks), dim3(kSetupThreads), 0,
+                          stream, perm, B, S, plan.nnz + 1, plan.live_bits, plan.full_bits, T * W, fk_adj, R, WR,
+                          kind == RT_MASK_NEIGHBOR ? 1 : 0, plan.fk_bits))
+    return st;
   const dim3 grid((T + kTileWarps - 1) / kTileWarps, T, B);
   const bool staged = WR <= kMaxStagedWords;
   const size_t fk_smem = sizeof(uint32_t) * RT_TILE * (size_t)(WR | 1);
-  if (kind == RT_MASK_COLUMN)
-    tile_mask_kernel<RT_MASK_COLUMN, false><<<grid, kTileWarps * 32, 0, stream>>>(perm, seq_row_ids, column_ids,
-                                                                          is_padding, fk_bits, S, R, WR, plan);
-  else if (kind == RT_MASK_FEATURE && staged)
-    tile_mask_kernel<RT_MASK_FEATURE, true><<<grid, kTileWarps * 32, fk_smem, stream>>>(perm, seq_row_ids, column_ids,
-                                                                                is_padding, fk_bits, S, R, WR, plan);
-  else if (kind == RT_MASK_FEATURE)
-    tile_mask_kernel<RT_MASK_FEATURE, false><<<grid, kTileWarps * 32, 0, stream>>>(perm, seq_row_ids, column_ids,
-                                                                           is_padding, fk_bits, S, R, WR, plan);
-  else if (kind == RT_MASK_NEIGHBOR && staged)
-    tile_mask_kernel<RT_MASK_NEIGHBOR, true><<<grid, kTileWarps * 32, fk_smem, stream>>>(perm, seq_row_ids, column_ids,
-                                                                                 is_padding, fk_bits, S, R, WR, plan);
-  else if (kind == RT_MASK_NEIGHBOR)
-    tile_mask_kernel<RT_MASK_NEIGHBOR, false><<<grid, kTileWarps * 32, 0, stream>>>(perm, seq_row_ids, column_ids,
-                                                                            is_padding, fk_bits, S, R, WR, plan);
-  else
-    tile_mask_kernel<RT_MASK_FULL, false><<<grid, kTileWarps * 32, 0, stream>>>(perm, seq_row_ids, column_ids,
-                                                                        is_padding, fk_bits, S, R, WR, plan);
+  using MaskKernel = void (*)(const uint16_t*, const uint16_t*, const int32_t*, const uint8_t*, const uint32_t*,
+                              int, int, int, rt_tile_plan);
+  MaskKernel mask_kernel = tile_mask_kernel<RT_MASK_FULL, false>;
+  if (kind == RT_MASK_COLUMN) mask_kernel = tile_mask_kernel<RT_MASK_COLUMN, false>;
+  else if (kind == RT_MASK_FEATURE) mask_kernel = staged ? tile_mask_kernel<RT_MASK_FEATURE, true>
+                                                         : tile_mask_kernel<RT_MASK_FEATURE, false>;
+  else if (kind == RT_MASK_NEIGHBOR) mask_kernel = staged ? tile_mask_kernel<RT_MASK_NEIGHBOR, true>
+                                                          : tile_mask_kernel<RT_MASK_NEIGHBOR, false>;
+  const bool uses_smem = (kind == RT_MASK_FEATURE || kind == RT_MASK_NEIGHBOR) && staged;
+  if (int st = launch_pdl("tile_mask_kernel launch", mask_kernel, grid, dim3(kTileWarps * 32),
+                          uses_smem ? fk_smem : 0, stream, perm, seq_row_ids, column_ids, is_padding, fk_bits, S, R,
+                          WR, plan))
+    return st;
   {
     const size_t bits_bytes = 2 * sizeof(uint32_t) * (size_t)plan.tiles * plan.words;  // one sample
     const size_t smem = bits_bytes <= (size_t)kListSmemBytes ? bits_bytes : 0;
@@ -431,7 +433,8 @@ int launch_build_tile_plan(const uint16_t* perm, const uint16_t* seq_row_ids, co
       if (e != cudaSuccess) return cuda_failure(e, "cudaFuncSetAttribute(tile_list_kernel)");
       list_configured[dev] = true;
     }
-    tile_list_kernel<<<B, kListThreads, smem, stream>>>(plan);
+    if (int st = launch_pdl("tile_list_kernel launch", tile_list_kernel, dim3(B), dim3(kListThreads), smem, stream, plan))
+      return st;
   }
   return check_launch("tile plan kernels launch");
 }
