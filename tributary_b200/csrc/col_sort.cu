@@ -22,6 +22,8 @@ constexpr int kThreads = 1024;
 __global__ void __launch_bounds__(kThreads) column_order_kernel(const int32_t* __restrict__ column_ids,
                                                                 const uint8_t* __restrict__ is_padding, int S,
                                                                 int n_pow2, uint16_t* __restrict__ perm) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   extern __shared__ unsigned long long keys[];
   const int b = blockIdx.x;
   const int32_t* col = column_ids + (size_t)b * S;
@@ -77,7 +79,10 @@ extern "C" int rt_column_order_device(const int32_t* column_ids, const uint8_t* 
     if (e != cudaSuccess) return cuda_failure(e, "cudaFuncSetAttribute(column_order_kernel)");
     configured[dev] = true;
   }
-  colsort::column_order_kernel<<<batch, colsort::kThreads, smem, static_cast<cudaStream_t>(stream)>>>(
-      column_ids, is_padding, seq_len, n_pow2, perm);
+  {
+    if (int st_pdl = launch_pdl("column_order_kernel launch", colsort::column_order_kernel, dim3(batch),
+        dim3(colsort::kThreads), smem, static_cast<cudaStream_t>(stream), column_ids, is_padding, seq_len,
+        n_pow2, perm)) return st_pdl;
+  }
   return check_launch("column_order_kernel launch");
 }

@@ -60,6 +60,8 @@ template <int G>
 __global__ void __launch_bounds__(256) rms_norm_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
                                                        long long rows, int d, float eps, uint16_t* __restrict__ y,
                                                        float* __restrict__ rstd) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -100,6 +102,8 @@ __global__ void __launch_bounds__(256) rms_norm_bwd_kernel(const uint16_t* __res
                                                            const float* __restrict__ gamma,
                                                            const float* __restrict__ rstd, long long rows, int d,
                                                            float* __restrict__ dx, float* __restrict__ part) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   __shared__ float sred[8][kMaxD / 8 + 1];  // per warp, one float per group slot (reduced below)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int groups = d >> 3;
@@ -167,6 +171,8 @@ __global__ void __launch_bounds__(256) rms_norm_bwd_kernel(const uint16_t* __res
 // deterministic.
 __global__ void __launch_bounds__(256) sum_partials_kernel(const float* __restrict__ part, int nparts, int d,
                                                            float* __restrict__ out) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   __shared__ float sw[8][32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + lane;
@@ -186,6 +192,8 @@ __global__ void __launch_bounds__(256) sum_partials_kernel(const float* __restri
 __global__ void __launch_bounds__(256) gate_residual_kernel(const float* __restrict__ x, const uint16_t* __restrict__ o,
                                                             const uint16_t* __restrict__ gate, long long n8, float scale,
                                                             float* __restrict__ y) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
     const F8 xv = load_f32x8(x + i * 8), ov = load_bf16x8(o + i * 8), gv = load_bf16x8(gate + i * 8);
     F8 r;
@@ -200,6 +208,8 @@ __global__ void __launch_bounds__(256) gate_residual_bwd_kernel(const float* __r
                                                                 const uint16_t* __restrict__ gate, long long n8,
                                                                 float scale, uint16_t* __restrict__ d_o,
                                                                 uint16_t* __restrict__ d_gate) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
     const F8 g = load_f32x8(dy + i * 8), ov = load_bf16x8(o + i * 8), gv = load_bf16x8(gate + i * 8);
     F8 a, b;
@@ -216,6 +226,8 @@ __global__ void __launch_bounds__(256) gate_residual_bwd_kernel(const float* __r
 
 __global__ void __launch_bounds__(256) residual_add_kernel(const float* __restrict__ x, const uint16_t* __restrict__ h,
                                                            long long n8, float scale, float* __restrict__ y) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
     const F8 xv = load_f32x8(x + i * 8), hv = load_bf16x8(h + i * 8);
     F8 r;
@@ -227,6 +239,8 @@ __global__ void __launch_bounds__(256) residual_add_kernel(const float* __restri
 
 __global__ void __launch_bounds__(256) residual_add_bwd_kernel(const float* __restrict__ dy, long long n8, float scale,
                                                                uint16_t* __restrict__ dh) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
     F8 g = load_f32x8(dy + i * 8);
 #pragma unroll
@@ -238,6 +252,8 @@ __global__ void __launch_bounds__(256) residual_add_bwd_kernel(const float* __re
 // u [rows][2f]: a = u[:, :f], b = u[:, f:]; h [rows][f]
 __global__ void __launch_bounds__(256) swiglu_kernel(const uint16_t* __restrict__ u, long long rows, int f,
                                                      uint16_t* __restrict__ h) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   const int g8 = f >> 3;
   const long long n8 = rows * g8;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
@@ -253,6 +269,8 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const uint16_t* __restrict_
 
 __global__ void __launch_bounds__(256) swiglu_bwd_kernel(const uint16_t* __restrict__ dh, const uint16_t* __restrict__ u,
                                                          long long rows, int f, uint16_t* __restrict__ du) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   const int g8 = f >> 3;
   const long long n8 = rows * g8;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
@@ -298,8 +316,14 @@ extern "C" int rt_rms_norm(const float* x, const float* gamma, int64_t rows, int
   const int blocks = (int)((rows + 7) / 8);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int gpl = (d / 8 + 31) / 32;  // groups of 8 per lane
-  if (gpl <= 2) layer::rms_norm_kernel<2><<<blocks, 256, 0, s>>>(x, gamma, rows, d, eps, y, rstd);
-  else layer::rms_norm_kernel<4><<<blocks, 256, 0, s>>>(x, gamma, rows, d, eps, y, rstd);
+  if (gpl <= 2) {
+   if (int st_pdl = launch_pdl("rms_norm_kernel launch", layer::rms_norm_kernel<2>, dim3(blocks), dim3(256), 0,
+       s, x, gamma, rows, d, eps, y, rstd)) return st_pdl;
+ }
+  else {
+   if (int st_pdl = launch_pdl("rms_norm_kernel launch", layer::rms_norm_kernel<4>, dim3(blocks), dim3(256), 0,
+       s, x, gamma, rows, d, eps, y, rstd)) return st_pdl;
+ }
   return check_launch("rms_norm_kernel launch");
 }
 
@@ -322,10 +346,19 @@ extern "C" int rt_rms_norm_bwd(const uint16_t* dy, const float* x, const float* 
   const int blocks = layer::kNormBwdBlocks;
   float* part = static_cast<float*>(workspace);
   const int gpl = (d / 8 + 31) / 32;
-  if (gpl <= 2) layer::rms_norm_bwd_kernel<2><<<blocks, 256, 0, s>>>(dy, x, gamma, rstd, rows, d, dx, part);
-  else layer::rms_norm_bwd_kernel<4><<<blocks, 256, 0, s>>>(dy, x, gamma, rstd, rows, d, dx, part);
+  if (gpl <= 2) {
+   if (int st_pdl = launch_pdl("rms_norm_bwd_kernel launch", layer::rms_norm_bwd_kernel<2>, dim3(blocks),
+       dim3(256), 0, s, dy, x, gamma, rstd, rows, d, dx, part)) return st_pdl;
+ }
+  else {
+   if (int st_pdl = launch_pdl("rms_norm_bwd_kernel launch", layer::rms_norm_bwd_kernel<4>, dim3(blocks),
+       dim3(256), 0, s, dy, x, gamma, rstd, rows, d, dx, part)) return st_pdl;
+ }
   if (int st = check_launch("rms_norm_bwd_kernel launch")) return st;
-  layer::sum_partials_kernel<<<(d + 31) / 32, 256, 0, s>>>(part, blocks, d, dgamma);
+  {
+    if (int st_pdl = launch_pdl("sum_partials_kernel launch", layer::sum_partials_kernel, dim3((d + 31) / 32),
+        dim3(256), 0, s, part, blocks, d, dgamma)) return st_pdl;
+  }
   return check_launch("sum_partials_kernel launch");
 }
 
@@ -337,8 +370,11 @@ extern "C" int rt_gate_residual(const float* x, const uint16_t* o, const uint16_
   if (!ok16(x) || !ok16(o) || !ok16(gate) || !ok16(y)) return RT_ERR_INVALID_ARGUMENT;
   DeviceGuard guard(x);
   if (guard.status() != RT_OK) return guard.status();
-  layer::gate_residual_kernel<<<layer::grid_for(n / 8, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      x, o, gate, n / 8, scale, y);
+  {
+    if (int st_pdl = launch_pdl("gate_residual_kernel launch", layer::gate_residual_kernel,
+        dim3(layer::grid_for(n / 8, 256)), dim3(256), 0, static_cast<cudaStream_t>(stream), x, o, gate, n / 8,
+        scale, y)) return st_pdl;
+  }
   return check_launch("gate_residual_kernel launch");
 }
 
@@ -350,8 +386,11 @@ extern "C" int rt_gate_residual_bwd(const float* dy, const uint16_t* o, const ui
   if (!ok16(dy) || !ok16(o) || !ok16(gate) || !ok16(d_o) || !ok16(d_gate)) return RT_ERR_INVALID_ARGUMENT;
   DeviceGuard guard(dy);
   if (guard.status() != RT_OK) return guard.status();
-  layer::gate_residual_bwd_kernel<<<layer::grid_for(n / 8, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      dy, o, gate, n / 8, scale, d_o, d_gate);
+  {
+    if (int st_pdl = launch_pdl("gate_residual_bwd_kernel launch", layer::gate_residual_bwd_kernel,
+        dim3(layer::grid_for(n / 8, 256)), dim3(256), 0, static_cast<cudaStream_t>(stream), dy, o, gate, n / 8,
+        scale, d_o, d_gate)) return st_pdl;
+  }
   return check_launch("gate_residual_bwd_kernel launch");
 }
 
@@ -362,8 +401,10 @@ extern "C" int rt_swiglu(const uint16_t* u, int64_t rows, int32_t f, uint16_t* h
   if (!ok16(u) || !ok16(h)) return RT_ERR_INVALID_ARGUMENT;
   DeviceGuard guard(u);
   if (guard.status() != RT_OK) return guard.status();
-  layer::swiglu_kernel<<<layer::grid_for(rows * (f / 8), 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(u, rows, f,
-                                                                                                            h);
+  {
+    if (int st_pdl = launch_pdl("swiglu_kernel launch", layer::swiglu_kernel, dim3(layer::grid_for(rows * (f /
+        8), 256)), dim3(256), 0, static_cast<cudaStream_t>(stream), u, rows, f, h)) return st_pdl;
+  }
   return check_launch("swiglu_kernel launch");
 }
 
@@ -375,8 +416,10 @@ extern "C" int rt_swiglu_bwd(const uint16_t* dh, const uint16_t* u, int64_t rows
   if (!ok16(dh) || !ok16(u) || !ok16(du)) return RT_ERR_INVALID_ARGUMENT;
   DeviceGuard guard(u);
   if (guard.status() != RT_OK) return guard.status();
-  layer::swiglu_bwd_kernel<<<layer::grid_for(rows * (f / 8), 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      dh, u, rows, f, du);
+  {
+    if (int st_pdl = launch_pdl("swiglu_bwd_kernel launch", layer::swiglu_bwd_kernel, dim3(layer::grid_for(rows
+        * (f / 8), 256)), dim3(256), 0, static_cast<cudaStream_t>(stream), dh, u, rows, f, du)) return st_pdl;
+  }
   return check_launch("swiglu_bwd_kernel launch");
 }
 
@@ -387,8 +430,10 @@ extern "C" int rt_residual_add(const float* x, const uint16_t* h, int64_t n, flo
   if (!ok16(x) || !ok16(h) || !ok16(y)) return RT_ERR_INVALID_ARGUMENT;
   DeviceGuard guard(x);
   if (guard.status() != RT_OK) return guard.status();
-  layer::residual_add_kernel<<<layer::grid_for(n / 8, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, h, n / 8,
-                                                                                                        scale, y);
+  {
+    if (int st_pdl = launch_pdl("residual_add_kernel launch", layer::residual_add_kernel, dim3(layer::grid_for(n
+        / 8, 256)), dim3(256), 0, static_cast<cudaStream_t>(stream), x, h, n / 8, scale, y)) return st_pdl;
+  }
   return check_launch("residual_add_kernel launch");
 }
 
@@ -399,7 +444,10 @@ extern "C" int rt_residual_add_bwd(const float* dy, int64_t n, float scale, uint
   if (!ok16(dy) || !ok16(dh)) return RT_ERR_INVALID_ARGUMENT;
   DeviceGuard guard(dy);
   if (guard.status() != RT_OK) return guard.status();
-  layer::residual_add_bwd_kernel<<<layer::grid_for(n / 8, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      dy, n / 8, scale, dh);
+  {
+    if (int st_pdl = launch_pdl("residual_add_bwd_kernel launch", layer::residual_add_bwd_kernel,
+        dim3(layer::grid_for(n / 8, 256)), dim3(256), 0, static_cast<cudaStream_t>(stream), dy, n / 8, scale,
+        dh)) return st_pdl;
+  }
   return check_launch("residual_add_bwd_kernel launch");
 }

@@ -81,6 +81,8 @@ __global__ void __launch_bounds__(32 * kWarps) qk_prepare_kernel(const uint16_t*
                                                                  const float* __restrict__ tau, int B, int H, int S,
                                                                  uint16_t* __restrict__ q, uint16_t* __restrict__ k,
                                                                  uint16_t* __restrict__ v, float* __restrict__ rnorm) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   constexpr int kL = DH / 8;      // lanes per row
   constexpr int kRows = 32 / kL;  // rows per warp instruction
   constexpr int kBatch = 6;       // instructions whose loads are issued together
@@ -156,6 +158,8 @@ __global__ void __launch_bounds__(32 * kWarps) qk_prepare_bwd_kernel(
     const uint16_t* __restrict__ qkv, const uint16_t* __restrict__ perm, const float* __restrict__ tau,
     const float* __restrict__ rnorm, int B, int H, int S, uint16_t* __restrict__ dqkv,
     float* __restrict__ dtau_rows) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const long long t = (long long)blockIdx.x * kWarps + (threadIdx.x >> 5);
   if (t >= (long long)B * S) return;
@@ -181,6 +185,8 @@ template <int DH, bool kToTokens>
 __global__ void __launch_bounds__(32 * kWarps) heads_reorder_kernel(const uint16_t* __restrict__ src,
                                                                     const uint16_t* __restrict__ perm, int B, int H,
                                                                     int S, uint16_t* __restrict__ dst) {
+  pdl_wait();  // the previous kernel on the stream has completed (launch_pdl)
+  pdl_trigger();
   constexpr int kL = DH / 8;
   constexpr int kRows = 32 / kL;
   constexpr int kBatch = 4;
@@ -240,11 +246,15 @@ extern "C" int rt_qk_prepare(const uint16_t* qkv, const uint16_t* perm, const fl
   const unsigned grid = tok::blocks_for((long long)batch * seq_len);
   auto s = static_cast<cudaStream_t>(stream);
   if (head_dim == 64)
-    tok::qk_prepare_kernel<64><<<grid, 32 * tok::kWarps, 0, s>>>(qkv, perm, tau, batch, heads, seq_len, q, k, v,
-                                                                 rnorm);
+    {
+      if (int st_pdl = launch_pdl("qk_prepare_kernel launch", tok::qk_prepare_kernel<64>, dim3(grid), dim3(32 *
+          tok::kWarps), 0, s, qkv, perm, tau, batch, heads, seq_len, q, k, v, rnorm)) return st_pdl;
+    }
   else
-    tok::qk_prepare_kernel<32><<<grid, 32 * tok::kWarps, 0, s>>>(qkv, perm, tau, batch, heads, seq_len, q, k, v,
-                                                                 rnorm);
+    {
+      if (int st_pdl = launch_pdl("qk_prepare_kernel launch", tok::qk_prepare_kernel<32>, dim3(grid), dim3(32 *
+          tok::kWarps), 0, s, qkv, perm, tau, batch, heads, seq_len, q, k, v, rnorm)) return st_pdl;
+    }
   return check_launch("qk_prepare_kernel launch");
 }
 
@@ -261,11 +271,17 @@ extern "C" int rt_qk_prepare_bwd(const uint16_t* dq, const uint16_t* dk, const u
   const unsigned grid = tok::blocks_for((long long)batch * seq_len);
   auto s = static_cast<cudaStream_t>(stream);
   if (head_dim == 64)
-    tok::qk_prepare_bwd_kernel<64><<<grid, 32 * tok::kWarps, 0, s>>>(dq, dk, dv, qkv, perm, tau, rnorm, batch,
-                                                                     heads, seq_len, dqkv, dtau_rows);
+    {
+      if (int st_pdl = launch_pdl("qk_prepare_bwd_kernel launch", tok::qk_prepare_bwd_kernel<64>, dim3(grid),
+          dim3(32 * tok::kWarps), 0, s, dq, dk, dv, qkv, perm, tau, rnorm, batch, heads, seq_len, dqkv,
+          dtau_rows)) return st_pdl;
+    }
   else
-    tok::qk_prepare_bwd_kernel<32><<<grid, 32 * tok::kWarps, 0, s>>>(dq, dk, dv, qkv, perm, tau, rnorm, batch,
-                                                                     heads, seq_len, dqkv, dtau_rows);
+    {
+      if (int st_pdl = launch_pdl("qk_prepare_bwd_kernel launch", tok::qk_prepare_bwd_kernel<32>, dim3(grid),
+          dim3(32 * tok::kWarps), 0, s, dq, dk, dv, qkv, perm, tau, rnorm, batch, heads, seq_len, dqkv,
+          dtau_rows)) return st_pdl;
+    }
   return check_launch("qk_prepare_bwd_kernel launch");
 }
 
@@ -282,9 +298,15 @@ int heads_reorder(const uint16_t* src, const uint16_t* perm, int32_t batch, int3
   const unsigned grid = tok::blocks_for((long long)batch * seq_len);
   auto s = static_cast<cudaStream_t>(stream);
   if (head_dim == 64)
-    tok::heads_reorder_kernel<64, kToTokens><<<grid, 32 * tok::kWarps, 0, s>>>(src, perm, batch, heads, seq_len, dst);
+    {
+      if (int st_pdl = launch_pdl("heads_reorder_kernel launch", tok::heads_reorder_kernel<64, kToTokens>,
+          dim3(grid), dim3(32 * tok::kWarps), 0, s, src, perm, batch, heads, seq_len, dst)) return st_pdl;
+    }
   else
-    tok::heads_reorder_kernel<32, kToTokens><<<grid, 32 * tok::kWarps, 0, s>>>(src, perm, batch, heads, seq_len, dst);
+    {
+      if (int st_pdl = launch_pdl("heads_reorder_kernel launch", tok::heads_reorder_kernel<32, kToTokens>,
+          dim3(grid), dim3(32 * tok::kWarps), 0, s, src, perm, batch, heads, seq_len, dst)) return st_pdl;
+    }
   return check_launch("heads_reorder_kernel launch");
 }
 }  // namespace
