@@ -112,13 +112,16 @@ __device__ __noinline__ void fix_row(long long r, const uint16_t* __restrict__ q
 //                one of two slots
 //   warp 1       PV issuer: O += P_g V_g into the item's O buffer (two,
 //                alternating by item), in tile order
-//   warp 18      S issuer: S_g = Q K_g^T into S buffer g % 3 once PV_{g-3},
+//   warp 22      S issuer: S_g = Q K_g^T into S buffer g % 3 once PV_{g-3},
 //                which reads P_{g-3} from that buffer, has completed
 //   warps 2..5   epilogue warpgroup: diagonal logits two items ahead, then
 //                O / l -> bf16 and lse per item
-//   warps 6..17  softmax: three sets of 4 warps (one per TMEM lane quadrant);
-//                set s takes the global tiles g with g % 3 == s; thread =
-//                query row, the row's 128 columns in four 32-column chunks
+//   warps 6..21  softmax: two groups of eight warps, group q taking the
+//                tiles g with g % 2 == q; in a group, two warps per TMEM
+//                lane quadrant, each owning a 64-column slice (two 32-column
+//                chunks) of its 32 rows (thread = query row). P of a chunk
+//                is packed over the first 16 of its 32 columns, so no warp
+//                writes columns another warp has still to read
 // Exponent reference: each row uses its own diagonal logit s_ii = q_i . k_i
 // (always live), p = exp2(c (s - s_ii) - kRefShift): the largest term is at
 // least 2^-kRefShift, so nothing that matters underflows, and no online max
@@ -127,23 +130,39 @@ __device__ __noinline__ void fix_row(long long r, const uint16_t* __restrict__ q
 // logit spread above about (100 + kRefShift)/c, impossible for L2-normalised
 // q, k) is recomputed exactly by the epilogue warp that finds it (fix_row).
 // TMEM (512 columns): S buffers [0,128), [128,256), [256,384) fp32 with P_g
-// written as bf16 pairs over columns [0,64) of its buffer, O buffers
-// [384, 384+DH) and [384+DH, 384+2DH).
+// written as bf16 pairs over columns [32 c, 32 c + 16) of its buffer for the
+// 32-column chunk c, O buffers [384, 384+DH) and [384+DH, 384+2DH).
 // ---------------------------------------------------------------------------
-constexpr int kSets = 3;
-constexpr int kSetWarps = 4;
-constexpr int kSoftmaxWarps = kSets * kSetWarps;
+constexpr int kSBufs = 3;        // S / P buffers: tiles in flight between the MMAs and the softmax
+constexpr int kSliceWarps = 4;   // softmax warps per lane quadrant
+constexpr int kSoftmaxWarps = 4 * kSliceWarps;
+// Softmax groups: group q takes the tiles g with g % kGroups == q, so one
+// group's exponentials overlap the other's barrier hand-offs. Measured at the
+// B=8, S=4096, H=16, Dh=64 workload: 1 group (all sixteen warps on every
+// tile) 1.352 ms for the four kinds, 2 groups 1.267 ms.
+constexpr int kGroups = 2;
+constexpr int kGroupWarps = kSoftmaxWarps / kGroups;
+constexpr int kChunks = kGroups;        // 32-column chunks per warp and tile
+// S-ready barriers, one per (buffer, group): tile g signals barrier
+// (g % kSBufs, g % kGroups), which comes round again every kStBars tiles
+// because kSBufs and kGroups are coprime
+constexpr int kStBars = kSBufs * kGroups;
+static_assert(kGroups == 1 || kGroups == 2, "kGroups must divide the 4 slices and be coprime with kSBufs");
 constexpr int kEpiWarps = 4;
 constexpr int kSIssueWarp = 2 + kEpiWarps + kSoftmaxWarps;  // issues the S MMAs; warp 1 issues PV
 constexpr int kMainThreads = 32 * (kSIssueWarp + 1);
 constexpr int kMainTmemCols = 512;
-constexpr int kOMain = kSets * 128;
+constexpr int kOMain = kSBufs * 128;
 constexpr int kStages = 4;
 constexpr int kInfoRing = 8;
 constexpr int kMaskBytes = RT_TILE * 16;
 // tile-info word: kt (bits 0-15), fully live (16), first tile of its item (17),
 // last tile of its item (18)
 constexpr uint32_t kInfoFull = 1u << 16, kInfoFirst = 1u << 17, kInfoLast = 1u << 18;
+
+// TMEM column (within an S buffer) of the bf16 pairs of P for keys
+// [16 ks, 16 ks + 16): chunk ks / 2, second half of its packed run if ks is odd.
+__device__ __forceinline__ uint32_t p_col(int ks) { return (uint32_t)((ks >> 1) * 32 + (ks & 1) * 8); }
 
 template <int DH>
 struct MainCfg {
@@ -164,7 +183,7 @@ struct MainCfg {
 struct __align__(8) MainBarriers {
   uint64_t q_full[2], q_empty[2];
   uint64_t kv_full[kStages], kv_empty[kStages];
-  uint64_t st_full[kSets], p_full[kSets], pv_done[kSets];
+  uint64_t st_full[kStBars], p_full[kSBufs], pv_done[kSBufs];
   uint64_t item_done[2], o_free[2];
   uint64_t sdiag_full[2], lsum_full[2];
   uint64_t drain, drain_s;
@@ -217,7 +236,7 @@ __global__ void __launch_bounds__(kMainThreads, 1)
   __shared__ int abort_flag;
   __shared__ uint32_t s_info[kInfoRing];
   __shared__ float s_sdiag[2][RT_TILE];
-  __shared__ float s_lpart[2][kSets][RT_TILE];
+  __shared__ float s_lpart[2][kSliceWarps][RT_TILE];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -246,9 +265,9 @@ __global__ void __launch_bounds__(kMainThreads, 1)
       mbar_init(&bars.kv_full[i], 1);
       mbar_init(&bars.kv_empty[i], 1);
     }
-    for (int i = 0; i < kSets; ++i) {
-      mbar_init(&bars.st_full[i], 1);
-      mbar_init(&bars.p_full[i], kSetWarps);
+    for (int i = 0; i < kStBars; ++i) mbar_init(&bars.st_full[i], 1);
+    for (int i = 0; i < kSBufs; ++i) {
+      mbar_init(&bars.p_full[i], kGroupWarps);
       mbar_init(&bars.pv_done[i], 1);
     }
     mbar_init(&bars.drain, 1);
@@ -331,7 +350,7 @@ __global__ void __launch_bounds__(kMainThreads, 1)
     // ---------------- PV issue: the whole warp waits, one elected lane issues ----------------
     // Two warps issue MMAs so that each one's barrier waits overlap the other's
     // MMAs: this one O += P_g V_g in tile order, kSIssueWarp the S tiles. The
-    // S tile g lands in the buffer P_{g - kSets} occupies, so the S warp waits
+    // S tile g lands in the buffer P_{g - kSBufs} occupies, so the S warp waits
     // for pv_done (committed after that PV) before issuing it.
     {
       const bool leader = elect_one_sync();
@@ -345,17 +364,17 @@ __global__ void __launch_bounds__(kMainThreads, 1)
         const int ob = kP & 1;
         if (kP >= 2 && !(ok = mbar_wait_warp(&bars.o_free[ob], ((kP - 2) >> 1) & 1, &abort_flag))) break;
         for (int t = 0; ok && t < n; ++t, ++g) {
-          const int set = g % kSets;
-          if (!(ok = mbar_wait_warp(&bars.p_full[set], (g / kSets) & 1, &abort_flag))) break;
+          const int buf = g % kSBufs;
+          if (!(ok = mbar_wait_warp(&bars.p_full[buf], (g / kSBufs) & 1, &abort_flag))) break;
           tc_fence_after();
           // V is MN-major: +kRowBytes (16-byte units) per 16 keys
           const uint64_t vd = sdesc(smem_u32(smem + C::kVOff + (g % kStages) * C::kTileBytes), 0, C::kSBO, C::kSwizzle);
           if (leader) {
 #pragma unroll
             for (int ks = 0; ks < RT_TILE / 16; ++ks)  // O += P_g V_g
-              mma_ts(tmem + kOMain + ob * DH, tmem + set * 128 + ks * 8, vd + ks * C::kRowBytes, idesc_o,
+              mma_ts(tmem + kOMain + ob * DH, tmem + buf * 128 + p_col(ks), vd + ks * C::kRowBytes, idesc_o,
                      (t > 0 || ks > 0) ? 1u : 0u);
-            mma_commit(&bars.pv_done[set]);
+            mma_commit(&bars.pv_done[buf]);
             mma_commit(&bars.kv_empty[g % kStages]);
             if (t == n - 1) mma_commit(&bars.item_done[ob]);
           }
@@ -393,17 +412,17 @@ __global__ void __launch_bounds__(kMainThreads, 1)
       if (tS == 0 && !(ok = mbar_wait_warp(&bars.q_full[kS & 1], (kS >> 1) & 1, &abort_flag))) break;
       const int st = gS % kStages;
       if (!(ok = mbar_wait_warp(&bars.kv_full[st], (gS / kStages) & 1, &abort_flag))) break;
-      // S_gS overwrites P_{gS - kSets}: wait until the PV that reads it has completed
-      if (gS >= kSets && !(ok = mbar_wait_warp(&bars.pv_done[gS % kSets], ((gS / kSets) - 1) & 1, &abort_flag)))
+      // S_gS overwrites P_{gS - kSBufs}: wait until the PV that reads it has completed
+      if (gS >= kSBufs && !(ok = mbar_wait_warp(&bars.pv_done[gS % kSBufs], ((gS / kSBufs) - 1) & 1, &abort_flag)))
         break;
       tc_fence_after();
       const uint64_t qd = sdesc(smem_u32(smem + C::kQOff + (kS & 1) * C::kTileBytes), 16, C::kSBO, C::kSwizzle);
       const uint64_t kd = sdesc(smem_u32(smem + C::kKOff + st * C::kTileBytes), 16, C::kSBO, C::kSwizzle);
-      const uint32_t d = tmem + (gS % kSets) * 128;
+      const uint32_t d = tmem + (gS % kSBufs) * 128;
       if (leader) {
 #pragma unroll
         for (int ks = 0; ks < DH / 16; ++ks) mma_ss(d, qd + ks * 2, kd + ks * 2, idesc_s, ks > 0 ? 1u : 0u);
-        mma_commit(&bars.st_full[gS % kSets]);
+        mma_commit(&bars.st_full[(gS % kSBufs) * kGroups + gS % kGroups]);
       }
       __syncwarp();
       ++tS;
@@ -437,9 +456,9 @@ __global__ void __launch_bounds__(kMainThreads, 1)
       if (!(ok = mbar_wait_warp(&bars.lsum_full[k & 1], (k >> 1) & 1, &abort_flag))) break;
       float l = 0.f;
 #pragma unroll
-      for (int s2 = 0; s2 < kSets; ++s2) l += s_lpart[k & 1][s2][row];
+      for (int w = 0; w < kSliceWarps; ++w) l += s_lpart[k & 1][w][row];
       const float sd = s_sdiag[k & 1][row];
-      if (k + 2 < n_items) put_sdiag(k + 2);  // sets finished item k: both buffers' readers are done
+      if (k + 2 < n_items) put_sdiag(k + 2);  // the softmax warps finished item k: both buffers' readers are done
       if (!(ok = mbar_wait_warp(&bars.item_done[k & 1], (k >> 1) & 1, &abort_flag))) break;
       tc_fence_after();
       uint32_t o[DH];
@@ -486,13 +505,14 @@ __global__ void __launch_bounds__(kMainThreads, 1)
     }
     tc_fence_before();
   } else {
-    // ---------------- softmax sets ----------------
+    // ---------------- softmax ----------------
     const int sw = warp - 2 - kEpiWarps;
-    const int set = sw / kSetWarps;
+    const int grp = sw / kGroupWarps;
+    const int part = sw >> 2;  // (group, column slice) of this warp: its row-sum partial
+    const int slice = (sw >> 2) % (4 / kGroups);  // this warp's kChunks * 32 columns of each tile
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
-    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
-    const uint32_t sbuf = lane_base + (uint32_t)(set * 128);
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(slice * kChunks * 32);
     const float c = scale_log2;
     const float2 c2 = make_float2(c, c);
     bool ok = true;
@@ -505,58 +525,58 @@ __global__ void __launch_bounds__(kMainThreads, 1)
       const float nref = -(s_sdiag[k & 1][row] * c + kRefShift);
       const float2 nm2 = make_float2(nref, nref);
       float2 lsum[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-      int t = (set - g % kSets + kSets) % kSets;  // first tile of this item owned by this set
-      for (; t < n; t += kSets) {
+      for (int t = (grp - g % kGroups + kGroups) % kGroups; t < n; t += kGroups) {
         const int gt = g + t;
-        const int u = gt / kSets;  // this set's tile count = phase of its barriers
-        if (!(ok = mbar_wait_warp(&bars.st_full[set], u & 1, &abort_flag))) break;
+        const int buf = gt % kSBufs;
+        if (!(ok = mbar_wait_warp(&bars.st_full[buf * kGroups + gt % kGroups], (gt / kStBars) & 1, &abort_flag)))
+          break;
         // S_gt issued implies its K / V / mask stage and tile info are in shared memory
         if (!(ok = mbar_wait_warp(&bars.kv_full[gt % kStages], (gt / kStages) & 1, &abort_flag))) break;
         tc_fence_after();
         const uint32_t info = s_info[gt % kInfoRing];
         const bool full = (info & kInfoFull) != 0;
-        uint4 mk = make_uint4(0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu, 0xFFFFFFFFu);
-        if (!full) mk = *reinterpret_cast<const uint4*>(smem + C::kMOff + (gt % kStages) * kMaskBytes + row * 16);
-        const uint32_t mw[4] = {mk.x, mk.y, mk.z, mk.w};
+        const uint8_t* mrow = smem + C::kMOff + (gt % kStages) * kMaskBytes + row * 16 + slice * kChunks * 4;
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {  // 32 columns; P of chunk ch lands in columns [16 ch, 16 ch + 16)
+        for (int ch = 0; ch < kChunks; ++ch) {
+          const uint32_t taddr = lane_base + (uint32_t)(buf * 128 + ch * 32);
+          const uint32_t mw = full ? 0xFFFFFFFFu : reinterpret_cast<const uint32_t*>(mrow)[ch];
           uint32_t pk[16];
-          // a 32 x 32 block with no live element: P = 0, nothing to load or exponentiate
-          if (!full && __all_sync(0xFFFFFFFFu, mw[ch] == 0u)) {
+          if (!full && __all_sync(0xFFFFFFFFu, mw == 0u)) {
+            // a 32 x 32 block with no live element: P = 0, nothing to load or exponentiate
 #pragma unroll
             for (int e = 0; e < 16; ++e) pk[e] = 0u;
-            tmem_st16(sbuf + ch * 16, pk);
-            continue;
-          }
-          uint32_t r[32];
-          tmem_ld32(sbuf + ch * 32, r);
-          tmem_wait_ld();
-          if (!full) {
+          } else {
+            uint32_t r[32];
+            tmem_ld32(taddr, r);
+            tmem_wait_ld();
+            if (!full) {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) r[e] = ((mw[ch] >> e) & 1u) ? r[e] : __float_as_uint(-INFINITY);
-          }
+              for (int e = 0; e < 32; ++e) r[e] = ((mw >> e) & 1u) ? r[e] : __float_as_uint(-INFINITY);
+            }
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
+            for (int e = 0; e < 32; e += 4) {
 #pragma unroll
-            for (int a = 0; a < 2; ++a) {
-              const float2 x =
-                  ffma2(make_float2(__uint_as_float(r[e + 2 * a]), __uint_as_float(r[e + 2 * a + 1])), c2, nm2);
-              // half of the exponentials on the MUFU, half on the FMA pipe
-              const float2 p = a == 0 ? make_float2(fast_exp2(x.x), fast_exp2(x.y)) : exp2_poly2(x);
-              lsum[a] = fadd2(lsum[a], p);
-              pk[(e >> 1) + a] = pack_bf16x2(p.x, p.y);
+              for (int a = 0; a < 2; ++a) {
+                const float2 x =
+                    ffma2(make_float2(__uint_as_float(r[e + 2 * a]), __uint_as_float(r[e + 2 * a + 1])), c2, nm2);
+                // half of the exponentials on the MUFU, half on the FMA pipe
+                const float2 p = a == 0 ? make_float2(fast_exp2(x.x), fast_exp2(x.y)) : exp2_poly2(x);
+                lsum[a] = fadd2(lsum[a], p);
+                pk[(e >> 1) + a] = pack_bf16x2(p.x, p.y);
+              }
             }
           }
-          tmem_st16(sbuf + ch * 16, pk);
+          // P of these 32 columns over the first 16 of them (already read)
+          tmem_st16(taddr, pk);
         }
         tmem_wait_st();
-        // S_gt completed after PV of this set's previous tile (one commit tracks
-        // every earlier MMA), so P_gt overwrites nothing that MMA still reads
+        // S_gt was issued after PV_{gt-3}, which read P_{gt-3} from this buffer,
+        // had completed, so P_gt overwrites nothing an MMA still reads
         tc_fence_before();
-        mbar_arrive_warp(&bars.p_full[set]);
+        mbar_arrive_warp(&bars.p_full[buf]);
       }
       g += n;
-      s_lpart[k & 1][set][row] = (lsum[0].x + lsum[0].y) + (lsum[1].x + lsum[1].y);
+      s_lpart[k & 1][part][row] = (lsum[0].x + lsum[0].y) + (lsum[1].x + lsum[1].y);
       mbar_arrive_warp(&bars.lsum_full[k & 1]);
     }
     tc_fence_before();
