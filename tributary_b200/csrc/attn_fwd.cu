@@ -559,8 +559,14 @@ __global__ void __launch_bounds__(kMainThreads, 1)
               for (int a = 0; a < 2; ++a) {
                 const float2 x =
                     ffma2(make_float2(__uint_as_float(r[e + 2 * a]), __uint_as_float(r[e + 2 * a + 1])), c2, nm2);
-                // half of the exponentials on the MUFU, half on the FMA pipe
-                const float2 p = a == 0 ? make_float2(fast_exp2(x.x), fast_exp2(x.y)) : exp2_poly2(x);
+                // three pairs in four on the MUFU, the fourth as the polynomial on the
+                // FMA and integer pipes: the polynomial costs about three times the
+                // instructions of a MUFU pair, and instruction issue, not the MUFU, is
+                // the softmax's limit (same-box forward A/B at B=8, S=4096, H=16,
+                // Dh=64, four kinds: half polynomial 1.267 ms, a quarter 1.178 ms,
+                // none 1.213 ms)
+                const float2 p = (((e >> 1) + a) & 3) != 3 ? make_float2(fast_exp2(x.x), fast_exp2(x.y))
+                                                          : exp2_poly2(x);
                 lsum[a] = fadd2(lsum[a], p);
                 pk[(e >> 1) + a] = pack_bf16x2(p.x, p.y);
               }
